@@ -1,0 +1,400 @@
+"""Benchmark: SECOND-style backbone forward on the B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one forward of the 12-layer sparse backbone over a batch of 4
+synthetic LiDAR-like voxel clouds (40,000 voxels each, [41,1600,1408],
+fp16 features with fp32 accumulation), including every kernel-map build
+(a fresh SparseConvTensor each step, as in inference).  Under torchrun each
+rank runs its own 4 samples (weak scaling; no inter-GPU traffic on the conv
+path) and the step time is the max over ranks.
+
+Prints one JSON line (rank 0).  `value` is input voxels/s with inputs
+resident in HBM; `e2e` is the same metric through the public API with the
+inputs copied from pinned host memory and the output features read back
+every step; `roofline` is the convolution kernel's algorithmic bytes/FLOPs
+per launch over its CUDA-event time; `cpu_baseline` is the CPU oracle (a
+numpy port of the reference's PyTorch CPU path) on the same workload.
+`--impl reference` times only that CPU path.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "SECOND backbone voxels/s at 1/2/4/8 B200; per-layer % of HBM/TC roofline"
+UNIT = "voxels/s"
+WORKLOAD = "config3_second_backbone_fp16"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return dict(FALLBACK_PEAKS, bf16_tflops_sustained=1400.0)
+
+
+# fp32 CUDA-core FFMA peak (no measured figure): 148 SM x 128 lanes x 2 x 1965 MHz
+FP32_SIMT_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def workload_for_rank(rank: int, batch: int = 4):
+    from trispconv_b200.testing import synthetic as syn
+
+    return syn.config3(seed=3 + 1000 * rank, batch=batch)
+
+
+# --------------------------------------------------------------------------
+# CPU baseline (oracle = numpy port of the reference's CPU path)
+# --------------------------------------------------------------------------
+
+
+def cpu_forward_time(wl, reps: int = 1) -> float:
+    import oracle
+
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle.run_layers(wl.indices, wl.features, wl.spatial_shape, wl.batch_size, wl.layers)
+    return (time.perf_counter() - t0) / reps
+
+
+def cpu_baseline(wl) -> dict:
+    secs = cpu_forward_time(wl)
+    return {"value": wl.n_voxels / secs, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"one full forward of the config-3 batch ({wl.batch_size} samples, {wl.n_voxels} voxels), "
+                      f"numpy oracle in fp32, {secs:.2f} s"}
+
+
+def run_reference(args) -> None:
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    wl = workload_for_rank(0).sample_slice(0, 1)  # bounded sample: one 40k-voxel cloud per step
+    for _ in range(args.warmup):
+        cpu_forward_time(wl)
+    times = [cpu_forward_time(wl) for _ in range(args.steps)]
+    secs = float(np.mean(times))
+    value = wl.n_voxels / secs
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch": wl.batch_size, "voxels": wl.n_voxels,
+                       "spatial_shape": wl.spatial_shape, "layers": 12, "device": "cpu"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{args.steps} forwards of one config-3 sample ({wl.n_voxels} voxels) "
+                                       "through the numpy port of the reference's CPU path, fp32"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# GPU arm
+# --------------------------------------------------------------------------
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = ROOT / "gpurun_out" / f"clocks_bench_{gpu_index}_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.out.parent.mkdir(exist_ok=True)
+            self.fh = open(self.out, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.fh.close()
+        sm, smax, reasons = [], [], set()
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names[1:], parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+class ConvProbe:
+    """Records CUDA events around every convolution launch and kernel-map
+    build (bench instrumentation only)."""
+
+    def __init__(self):
+        import torch
+
+        import trispconv_b200.pytorch.modules as M
+
+        self.torch = torch
+        self.M = M
+        self.records = []
+        self.enabled = False
+        self._orig_conv = M.conv_launch
+        self._orig_subm = M.generate_subm_indice_pairs
+        self._orig_strided = M.generate_strided_indice_pairs
+        M.conv_launch = self._conv
+        M.generate_subm_indice_pairs = self._wrap(self._orig_subm, "kmap_subm")
+        M.generate_strided_indice_pairs = self._wrap(self._orig_strided, "kmap_strided")
+
+    def _events(self):
+        s = self.torch.cuda.Event(enable_timing=True)
+        e = self.torch.cuda.Event(enable_timing=True)
+        return s, e
+
+    def _conv(self, features, weight, layout, bias, km, n_out, c_out, relu=False):
+        if not self.enabled:
+            return self._orig_conv(features, weight, layout, bias, km, n_out, c_out, relu)
+        s, e = self._events()
+        s.record()
+        out = self._orig_conv(features, weight, layout, bias, km, n_out, c_out, relu)
+        e.record()
+        self.records.append(dict(kind="conv", start=s, end=e, n_in=features.shape[0], c_in=features.shape[1],
+                                 n_out=n_out, c_out=c_out, km=km, k_vol=1 if km is None else km.k_vol,
+                                 elem=features.element_size()))
+        return out
+
+    def _wrap(self, fn, kind):
+        def inner(indices, *a, **k):
+            if not self.enabled:
+                return fn(indices, *a, **k)
+            s, e = self._events()
+            s.record()
+            data = fn(indices, *a, **k)
+            e.record()
+            self.records.append(dict(kind=kind, start=s, end=e, n_in=indices.shape[0], data=data))
+            return data
+        return inner
+
+
+def layer_table(records, peaks) -> list:
+    rows = []
+    hbm = peaks["hbm_gbs"] * 1e9
+    tc = peaks["bf16_tflops"] * 1e12
+    for r in records:
+        ms = r["start"].elapsed_time(r["end"])
+        if r["kind"] != "conv":
+            d = r["data"]
+            P = int(d.pair_num.sum())
+            n_out = len(d.out_indices)
+            byt = 16 * r["n_in"] + (16 * n_out if r["kind"] == "kmap_strided" else 0) + 4 * P * 2
+            rows.append(dict(kind=r["kind"], ms=ms, n_in=r["n_in"], n_out=n_out, pairs=P, bytes=byt,
+                             bound="hbm", frac=(byt / hbm) / (ms / 1e3)))
+            continue
+        km = r["km"]
+        P = int(km.meta[8:8 + km.k_vol].sum().item()) if (km is not None and km.meta is not None) else r["n_out"]
+        s = r["elem"]
+        flops = 2.0 * P * r["c_in"] * r["c_out"]
+        byt = (s * r["n_in"] * r["c_in"] + s * r["n_out"] * r["c_out"] + s * r["k_vol"] * r["c_in"] * r["c_out"]
+               + 4 * P + 4 * r["c_out"])
+        pipe = tc if s == 2 else FP32_SIMT_TFLOPS * 1e12
+        t_roof = max(byt / hbm, flops / pipe)
+        rows.append(dict(kind="conv", ms=ms, n_in=r["n_in"], n_out=r["n_out"], c_in=r["c_in"], c_out=r["c_out"],
+                         pairs=P, bytes=byt, flops=flops, bound="hbm" if byt / hbm >= flops / pipe else "tensor",
+                         frac=t_roof / (ms / 1e3)))
+    return rows
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    ws, rank, local = dist_env()
+    if ws > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if ws > 1 else 0)
+    torch.cuda.set_device(dev)
+
+    import trispconv_b200.pytorch as spconv
+    from trispconv_b200 import _lib
+    from trispconv_b200.testing import networks
+
+    peaks = load_peaks()
+    wl = workload_for_rank(rank)
+    net = networks.build_network(wl.layers, dev, torch.float16)
+    feats_d = torch.from_numpy(wl.features).to(dev)
+    idx_d = torch.from_numpy(wl.indices).to(dev)
+    feats_h = torch.from_numpy(wl.features).pin_memory()
+    idx_h = torch.from_numpy(wl.indices).pin_memory()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    probe = ConvProbe()
+
+    def forward_resident():
+        x = spconv.SparseConvTensor(feats_d, idx_d, wl.spatial_shape, wl.batch_size)
+        return net(x)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        forward_resident()
+    barrier()
+
+    # ---- timed region: K steps, device-resident inputs -------------------
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches0 = _lib.launch_count()
+    probe.enabled = True
+    barrier()
+    wall0 = time.perf_counter()
+    for i in range(args.steps):
+        flush.fill_(float(i))  # evict L2 (256 MiB > 126 MB) outside the timed events
+        starts[i].record()
+        y = forward_resident()
+        ends[i].record()
+    barrier()
+    wall = time.perf_counter() - wall0
+    probe.enabled = False
+    launches = _lib.launch_count() - launches0
+    clk = clocks.stop()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    local_ms = float(np.sum(step_ms))
+    t = torch.tensor([local_ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = ws * wl.n_voxels / (ms_per_step / 1e3)
+    _lib.check_device_status(dev)
+
+    rows = layer_table(probe.records, peaks)
+    n_rows_step = len(rows) // args.steps
+    step_rows = rows[:n_rows_step]
+    conv_rows = [r for r in rows if r["kind"] == "conv"]
+    conv_ms = sum(r["ms"] for r in conv_rows) / args.steps
+    conv_bytes = sum(r["bytes"] for r in conv_rows) / args.steps
+    conv_flops = sum(r["flops"] for r in conv_rows) / args.steps
+    n_conv = len(conv_rows) // args.steps
+    hbm_t = conv_bytes / (peaks["hbm_gbs"] * 1e9)
+    tc_t = conv_flops / (peaks["bf16_tflops"] * 1e12)
+    if hbm_t >= tc_t:
+        roof = {"bound": "hbm", "achieved": conv_bytes / n_conv / (conv_ms / n_conv / 1e3) / 1e9,
+                "peak": peaks["hbm_gbs"], "unit": "GB/s"}
+    else:
+        roof = {"bound": "tensor", "achieved": conv_flops / n_conv / (conv_ms / n_conv / 1e3) / 1e12,
+                "peak": peaks["bf16_tflops"], "unit": "TFLOP/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = None
+    roof["kernel"] = "k_conv_simt (output-stationary implicit GEMM), all 12 layers"
+    roof["algorithmic_bytes_per_launch"] = conv_bytes / n_conv
+    roof["algorithmic_flops_per_launch"] = conv_flops / n_conv
+    roof["ms_per_launch"] = conv_ms / n_conv
+    roof["peak_source"] = peaks["source"]
+
+    # ---- e2e through the public API with host buffers --------------------
+    e2e_steps = max(3, min(args.steps, 20))
+    h2d = feats_h.numel() * feats_h.element_size() + idx_h.numel() * idx_h.element_size()
+    barrier()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e2e_ms = 0.0
+    d2h = 0
+    for i in range(e2e_steps):
+        flush.fill_(float(i))
+        e_start.record()
+        f = feats_h.to(dev, non_blocking=True)
+        ix = idx_h.to(dev, non_blocking=True)
+        out = net(spconv.SparseConvTensor(f, ix, wl.spatial_shape, wl.batch_size))
+        res = out.features.cpu()
+        e_end.record()
+        e_end.synchronize()
+        e2e_ms += e_start.elapsed_time(e_end)
+        d2h = res.numel() * res.element_size()
+    t = torch.tensor([e2e_ms / e2e_steps], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = ws * wl.n_voxels / (float(t.item()) / 1e3)
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(wl)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": wl.batch_size, "voxels_per_gpu": wl.n_voxels,
+                       "spatial_shape": wl.spatial_shape, "layers": 12, "parallelism": f"batch-shard x{ws}",
+                       "l2": "flushed between steps (256 MiB write outside the timed events)"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": float(t.item())},
+            "gpu_launches": launches,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "wall_s_timed_region": wall,
+            "step_ms": [round(v, 4) for v in step_ms],
+            "layers": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in r.items()} for r in step_rows],
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

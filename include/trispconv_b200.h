@@ -1,0 +1,223 @@
+/*
+ * trispconv_b200 — C ABI of the B200 (sm_100a) sparse-convolution hot path.
+ *
+ * This library replaces the compute behind the reference's pure-Python
+ * `trispconv.pytorch` package (mrpulford/trispconv):
+ *   - indice-pair (kernel-map) generation   trispconv/pytorch/indices.py:67-259,
+ *                                           trispconv/pytorch/modules.py:175-213
+ *   - gather-GEMM-scatter convolution        trispconv/pytorch/functional.py:14-51,
+ *                                           trispconv/pytorch/triton_kernels.py:31-135
+ *
+ * Conventions
+ *   - Every pointer argument named *_dev / device buffer is CUDA device memory
+ *     allocated by the caller (the Python host uses torch's caching
+ *     allocator).  The library holds no device memory of its own.
+ *   - `stream` is a cudaStream_t passed as void*.  All work is enqueued on it;
+ *     no entry point synchronises the stream.
+ *   - Host-side problems (bad arguments, misaligned pointers, launch failures)
+ *     are returned as a TSC_ERR_* code; tsc_last_error() gives the message.
+ *   - Problems only the device can see (coordinates outside the grid, a full
+ *     hash table) are OR-ed into the caller's int64 status word as
+ *     TSC_STATUS_* bits.  The caller checks it at its next synchronisation.
+ *   - Coordinates are int32 rows [b, z, y, x] (16-byte rows, the reference's
+ *     SparseConvTensor.indices layout, trispconv/pytorch/tensor.py:23-25).
+ *   - Kernel offsets are numbered k = (kz*kH + ky)*kW + kx, the reference's
+ *     loop order (indices.py:92-94 and the itertools.product at :177).
+ *   - Gather maps are k-major int32 arrays map[k][row]; -1 means "no pair".
+ */
+#ifndef TRISPCONV_B200_H
+#define TRISPCONV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TSC_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TSC_API __attribute__((visibility("default")))
+#else
+#define TSC_API
+#endif
+
+/* Host-side return codes. */
+#define TSC_OK                 0
+#define TSC_ERR_INVALID_ARG    1
+#define TSC_ERR_WORKSPACE      2
+#define TSC_ERR_CUDA           3
+#define TSC_ERR_UNSUPPORTED    4
+#define TSC_ERR_GRID_TOO_LARGE 5
+
+/* Device status bits, OR-ed into the caller's int64 status word. */
+#define TSC_STATUS_KEY_RANGE      0x1  /* a coordinate lies outside [0,batch) x spatial_shape */
+#define TSC_STATUS_HASH_FULL      0x2  /* open-addressing table ran out of probes */
+#define TSC_STATUS_OVERFLOW_FULL  0x4  /* duplicate-pair overflow list ran out of room */
+
+/* Feature / weight element types. */
+#define TSC_F32  0
+#define TSC_F16  1
+#define TSC_BF16 2
+#define TSC_F64  3
+
+/* Conv flags. */
+#define TSC_CONV_RELU 0x1
+
+/* Weight layouts accepted by tsc_conv_forward. */
+#define TSC_W_KCC  0  /* (K, C_in, C_out): the reference's internal layout (weight.py:36) */
+#define TSC_W_KRSC 1  /* (C_out, kD, kH, kW, C_in): spconv KRSC, the modules' parameter */
+
+/* Layout of the per-kernel-map int64 "meta" buffer (length TSC_META_COUNTS + K). */
+#define TSC_META_N_OUT      0  /* number of output voxels (strided) */
+#define TSC_META_N_PART     1  /* input rows with at least one pair (strided) */
+#define TSC_META_N_OVERFLOW 3  /* entries in the duplicate-pair overflow list */
+#define TSC_META_STATUS     4  /* snapshot of the status word at the count step */
+#define TSC_META_COUNTS     8  /* pair_num[k], k = 0..K-1 */
+
+/* Geometry of one convolution.  For submanifold convs out_shape == in_shape,
+ * stride = 1, padding = 0.  Shapes are (D, H, W) = (z, y, x) extents. */
+typedef struct tsc_geometry {
+  int32_t batch;
+  int32_t in_shape[3];
+  int32_t out_shape[3];
+  int32_t ksize[3];
+  int32_t stride[3];
+  int32_t padding[3];
+  int32_t dilation[3];
+} tsc_geometry;
+
+/* ---- introspection -------------------------------------------------------- */
+TSC_API int tsc_abi_version(void);
+TSC_API const char* tsc_last_error(void);
+/* Number of CUDA kernels this library has launched in this process. */
+TSC_API unsigned long long tsc_launch_count(void);
+
+/* ---- submanifold kernel map ----------------------------------------------
+ * Replaces generate_subm_indice_pairs (indices.py:67-140) and its dense
+ * B*D*H*W lookup table (_build_hash_table, indices.py:54-64) with an
+ * open-addressing hash of packed (b,z,y,x) keys.
+ *
+ * gather_map[k][i] = row j whose coordinate equals coord(i) + (k - K//2)*d,
+ * or -1.  With duplicate coordinates j is the LAST such row (the reference's
+ * `table[encoded] = arange` write order).  meta[TSC_META_COUNTS + k] receives
+ * pair_num[k].  Requires batch*D*H*W <= 2^32 - 2. */
+TSC_API size_t tsc_subm_kmap_workspace(int64_t n);
+TSC_API int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo,
+                  void* workspace, size_t workspace_bytes,
+                  int32_t* gather_map, int64_t* meta, int64_t* status, void* stream);
+
+/* ---- strided kernel map --------------------------------------------------
+ * Replaces generate_strided_indice_pairs (indices.py:143-259).  The output
+ * set is found with an occupancy bitmap over the output grid (1 bit per
+ * cell) and a prefix popcount, which yields the reference's
+ * `torch.unique(sorted=True)` order (:219-220) without a sort.
+ *
+ * Step 1 (count): marks the bitmap, counts pairs per offset and the
+ * participating input rows, and writes meta[N_OUT], meta[N_PART] and
+ * meta[STATUS].  The caller reads meta to size the outputs of step 2.
+ * Step 2 (emit): writes the sorted output coordinates, the output-stationary
+ * gather map gather_map[k][o] (-1 prefilled by this call), the
+ * input-stationary scatter map scatter_map[k][i] = o or -1, and, for
+ * duplicate input coordinates only, (k, o, i) triples that did not fit the
+ * gather map into `overflow` (capacity overflow_cap triples; count in
+ * meta[N_OVERFLOW]).  The same workspace must be passed to both steps. */
+TSC_API size_t tsc_strided_kmap_workspace(const tsc_geometry* geo);
+TSC_API int tsc_strided_kmap_count(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
+                           void* workspace, size_t workspace_bytes,
+                           int64_t* meta, int64_t* status, void* stream);
+TSC_API int tsc_strided_kmap_emit(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
+                          void* workspace, size_t workspace_bytes, int64_t n_out,
+                          int32_t* out_indices, int32_t* gather_map, int32_t* scatter_map,
+                          int32_t* overflow, int64_t overflow_cap,
+                          int64_t* meta, int64_t* status, void* stream);
+
+/* ---- inverse kernel maps -------------------------------------------------
+ * Replace the pair swap of SparseInverseConvolution (modules.py:175-213).
+ *
+ * From a strided forward map: keeps the forward-input rows that have at
+ * least one pair (ascending row order, modules.py:178-182), writes their
+ * coordinates to out_indices[n_part][4], the inverse gather map
+ * inv_gather[k][r] = scatter_map[k][row_r], and compact[i] = r or -1.  When
+ * n_part == n_in the gather map is the scatter map itself; pass
+ * inv_gather == scatter_map to skip the copy. */
+TSC_API size_t tsc_inverse_kmap_workspace(int64_t n_in);
+TSC_API int tsc_inverse_kmap_strided(const int32_t* in_indices, int64_t n_in,
+                             const int32_t* scatter_map, int32_t k_vol, int64_t n_part,
+                             void* workspace, size_t workspace_bytes,
+                             int32_t* out_indices, int32_t* inv_gather, int32_t* compact,
+                             int64_t* status, void* stream);
+
+/* From a submanifold forward map (an inverse conv keyed on a SubM
+ * indice_key).  Step 1 flags every row that some pair reads, compacts them
+ * and writes meta[N_PART].  Step 2 writes out_indices, the transposed gather
+ * map inv_gather[k][compact[j]] = i for gather_map[k][i] = j, and duplicate
+ * overflow triples as in tsc_strided_kmap_emit. */
+TSC_API int tsc_inverse_kmap_subm_count(const int32_t* gather_map, int32_t k_vol, int64_t n,
+                                void* workspace, size_t workspace_bytes,
+                                int32_t* compact, int64_t* meta, int64_t* status, void* stream);
+TSC_API int tsc_inverse_kmap_subm_emit(const int32_t* in_indices, const int32_t* gather_map,
+                               int32_t k_vol, int64_t n, const int32_t* compact, int64_t n_part,
+                               int32_t* out_indices, int32_t* inv_gather,
+                               int32_t* overflow, int64_t overflow_cap,
+                               int64_t* meta, int64_t* status, void* stream);
+
+/* ---- pair lists in the reference's order ---------------------------------
+ * Materialises IndiceData.pairs_in / pairs_out (K lists of int64) as two
+ * flat int64 arrays of length sum(pair_num), k-major, from a map[k][idx]:
+ *   mode 0: for each k, idx ascending with map >= 0: in = map, out = idx
+ *           (submanifold, indices.py:123-124; inverse of strided)
+ *   mode 1: for each k, idx ascending with map >= 0: in = idx,
+ *           out = remap ? remap[map] : map
+ *           (strided, indices.py:235-240; inverse of submanifold)
+ * `capacity` is the length of pairs_in / pairs_out (sum of pair_num); no
+ * write goes past it. */
+TSC_API size_t tsc_pairs_workspace(int32_t k_vol, int64_t n);
+TSC_API int tsc_pairs_materialize(const int32_t* map, int32_t k_vol, int64_t n, int32_t mode,
+                          const int32_t* remap, int64_t* pairs_in, int64_t* pairs_out,
+                          int64_t capacity, void* workspace, size_t workspace_bytes,
+                          int64_t* status, void* stream);
+
+/* Builds a gather map (and duplicate overflow) from explicit pair lists, for
+ * IndiceData objects a user built by hand.  pairs are flat int64 arrays with
+ * per-offset offsets offsets[k]..offsets[k+1] (host array, K+1 entries). */
+TSC_API int tsc_gather_from_pairs(const int64_t* pairs_in, const int64_t* pairs_out,
+                          const int64_t* offsets_host, int32_t k_vol, int64_t n_out,
+                          int32_t* gather_map, int32_t* overflow, int64_t overflow_cap,
+                          int64_t* meta, int64_t* status, void* stream);
+
+/* ---- convolution ----------------------------------------------------------
+ * Output-stationary implicit GEMM replacing sparse_conv_forward
+ * (functional.py:14-51):
+ *   out[o, :] = sum_k features[gather_map[k][o], :] @ weight[k]  (+ bias, ReLU)
+ * in k order, fp32 accumulation, one store per output row, no atomics.
+ * features [n_in][c_in], weight (layout TSC_W_KCC or TSC_W_KRSC), bias
+ * [c_out] (or NULL) and out [n_out][c_out] all share `dtype`.  Reading the
+ * KRSC parameter in place replaces normalize_spconv_weight (weight.py:8-50)
+ * for K > 1; the 1x1x1 quirk (weight.py:29-34) is the same storage read as
+ * TSC_W_KCC.  gather_map NULL means the identity map
+ * (K == 1, n_in == n_out: the inverse 1x1x1 path, modules.py:162-173).
+ * overflow (capacity overflow_cap triples) and meta carry the
+ * duplicate-coordinate pairs of the kernel-map builders; the kernel reads
+ * their count from meta[TSC_META_N_OVERFLOW] on the device.  Pass NULL when
+ * the map cannot have any (submanifold maps). */
+TSC_API int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t c_in,
+                     const void* weight, int32_t weight_layout, const void* bias,
+                     const int32_t* gather_map, int32_t k_vol, int64_t n_out, int32_t c_out,
+                     const int32_t* overflow, int64_t overflow_cap, const int64_t* meta,
+                     void* out, int32_t flags, int64_t* status, void* stream);
+
+/* ---- dense scatter ---------------------------------------------------------
+ * SparseConvTensor.dense() (tensor.py:72-99): writes features into a zeroed
+ * (B, C, D, H, W) (channels_first = 1) or (B, D, H, W, C) tensor.  Rows with
+ * coordinates outside the grid set TSC_STATUS_KEY_RANGE and are skipped. */
+TSC_API int tsc_to_dense(const void* features, int32_t dtype, const int32_t* indices, int64_t n, int32_t c,
+                 int32_t batch, const int32_t* shape3, int32_t channels_first,
+                 void* out, int64_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRISPCONV_B200_H */

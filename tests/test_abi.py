@@ -1,0 +1,87 @@
+"""The C ABI (include/trispconv_b200.h) without a GPU: the library builds,
+loads, exports every declared symbol, and rejects bad arguments on the host
+before touching the device."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from trispconv_b200 import _lib as L
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "trispconv_b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^TSC_API\s+[\w\s\*]+?\b(tsc_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not L.LIB_PATH.exists():
+        from trispconv_b200.build import build
+
+        build()
+    return L.load()
+
+
+def test_header_declares_the_bound_symbols():
+    decl = declared_symbols()
+    assert len(decl) >= 17
+    assert set(decl) == set(L.EXPORTED), set(decl) ^ set(L.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    raw = ctypes.CDLL(str(L.LIB_PATH))
+    for name in declared_symbols():
+        assert hasattr(raw, name), name
+
+
+def test_abi_version_and_introspection(lib):
+    assert lib.tsc_abi_version() == 1
+    assert isinstance(L.launch_count(), int)
+    assert isinstance(L.last_error(), str)
+
+
+def test_workspace_sizes(lib):
+    assert lib.tsc_subm_kmap_workspace(0) == 8 << 8
+    assert lib.tsc_subm_kmap_workspace(1000) == 8 << 11          # 2n rounded up to 2^11
+    assert lib.tsc_subm_kmap_workspace(160000) == 8 << 19
+    g = L.make_geometry(4, (41, 1600, 1408), (21, 800, 704), (3, 3, 3), (2, 2, 2), (1, 1, 1))
+    ws = lib.tsc_strided_kmap_workspace(ctypes.byref(g))
+    bits = 4 * 21 * 800 * 704
+    assert ws >= 2 * (bits // 8)                                  # bitmap + word prefix
+    assert lib.tsc_pairs_workspace(27, 1000) > 0
+    assert lib.tsc_inverse_kmap_workspace(1000) > 0
+
+
+def test_host_side_argument_checks(lib):
+    """Rejected before any CUDA call, so this runs without a GPU."""
+    meta = ctypes.c_int64 * 64
+    m, s = meta(), meta()
+    bad = L.make_geometry(0, (4, 4, 4), (4, 4, 4), (3, 3, 3))
+    rc = lib.tsc_subm_kmap(None, 10, ctypes.byref(bad), None, 0, None, ctypes.addressof(m),
+                           ctypes.addressof(s), None)
+    assert rc == L.TSC_ERR_INVALID_ARG and "batch" in L.last_error()
+    g = L.make_geometry(1, (4, 4, 4), (4, 4, 4), (3, 3, 3))
+    rc = lib.tsc_subm_kmap(None, -1, ctypes.byref(g), None, 0, None, ctypes.addressof(m),
+                           ctypes.addressof(s), None)
+    assert rc == L.TSC_ERR_INVALID_ARG
+    big = L.make_geometry(1 << 20, (1 << 10, 1 << 10, 1 << 10), (4, 4, 4), (3, 3, 3))
+    rc = lib.tsc_subm_kmap(None, 1, ctypes.byref(big), None, 0, None, ctypes.addressof(m),
+                           ctypes.addressof(s), None)
+    assert rc == L.TSC_ERR_GRID_TOO_LARGE
+    rc = lib.tsc_conv_forward(None, 0, 10, 0, None, 0, None, None, 27, 10, 8, None, 0, None, None, 0,
+                              ctypes.addressof(s), None)
+    assert rc == L.TSC_ERR_INVALID_ARG
+    rc = lib.tsc_conv_forward(None, 0, 10, 4, None, 0, None, None, 27, 10, 8, None, 0, None, None, 0,
+                              ctypes.addressof(s), None)
+    assert rc == L.TSC_ERR_INVALID_ARG and "identity" in L.last_error()
+    rc = lib.tsc_pairs_materialize(None, 27, 10, 7, None, None, None, 5, None, 0, None, None)
+    assert rc == L.TSC_ERR_INVALID_ARG
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    with pytest.raises(L.LibraryMissing):
+        L.load(tmp_path / "nope.so")

@@ -1,0 +1,110 @@
+"""The five benchmark configurations at full size on the GPU.
+
+Kernel maps: SHA-256 digests of every layer's pair lists / out_indices,
+compared with the digests recorded from the reference itself
+(tests/golden/ref_digests.json) -- bit-exact at full size.
+Features: against the CPU oracle, fp32 at 1e-4 (configs 1, 2), fp16 at a
+scale-relative 1e-2 against the fp32 oracle (configs 3-5; configs 4 and 5 on
+a subset of samples / output rows to keep the oracle fast).
+"""
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from golden_util import ref_digests
+from gpu_util import assert_close_rel, capture_kmaps, np_, our_digest
+from trispconv_b200.testing import networks, synthetic as syn
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(wl, dev, dtype):
+    net = networks.build_network(wl.layers, dev, dtype)
+    with capture_kmaps() as seen:
+        y = net(networks.make_input(wl, dev))
+    torch.cuda.synchronize()
+    return y, seen
+
+
+def _check_digests(name, wl, seen):
+    ref = ref_digests()[name]
+    assert hashlib.sha256(wl.indices.tobytes()).hexdigest() == ref["input_sha256"], "generator drifted"
+    assert len(seen) == len(ref["layers"])
+    for i, (d, r) in enumerate(zip(seen, ref["layers"])):
+        assert len(d.out_indices) == r["n_out"], i
+        assert int(d.pair_num.sum()) == r["pairs"], i
+        assert our_digest(d) == r["digest"], f"layer {i} kernel map differs from the reference"
+
+
+def test_config1(cuda):
+    wl = syn.config1()
+    y, seen = _run(wl, cuda, torch.float32)
+    _check_digests("config1", wl, seen)
+    ref = oracle.run_layers(wl.indices, wl.features, wl.spatial_shape, wl.batch_size, wl.layers)
+    np.testing.assert_allclose(np_(y.features), ref.features, rtol=1e-4, atol=1e-4)
+
+
+def test_config2(cuda):
+    wl = syn.config2()
+    y, seen = _run(wl, cuda, torch.float32)
+    _check_digests("config2", wl, seen)
+    ref = oracle.run_layers(wl.indices, wl.features, wl.spatial_shape, wl.batch_size, wl.layers)
+    assert np.array_equal(np_(y.indices), ref.indices)
+    np.testing.assert_allclose(np_(y.features), ref.features, rtol=1e-4, atol=1e-4)
+
+
+def test_config3_second_backbone(cuda):
+    wl = syn.config3()
+    y, seen = _run(wl, cuda, torch.float16)
+    _check_digests("config3", wl, seen)
+    ref = oracle.run_layers(wl.indices, wl.features, wl.spatial_shape, wl.batch_size, wl.layers)
+    assert np.array_equal(np_(y.indices), ref.indices)
+    assert y.spatial_shape == [2, 200, 176]
+    assert_close_rel(np_(y.features.float()), ref.features, 1e-2, "SECOND backbone output")
+
+
+def test_config4_unet_kernel_maps(cuda):
+    wl = syn.config4()
+    y, seen = _run(wl, cuda, torch.float16)
+    _check_digests("config4", wl, seen)
+    assert y.features.shape == (wl.n_voxels, 32) and torch.isfinite(y.features).all()
+
+
+def test_config4_unet_features_one_sample(cuda):
+    wl = syn.config4().sample_slice(0, 1)
+    y, _ = _run(wl, cuda, torch.float16)
+    ref = oracle.run_layers(wl.indices, wl.features, wl.spatial_shape, wl.batch_size, wl.layers)
+    assert np.array_equal(np_(y.indices), ref.indices)
+    assert_close_rel(np_(y.features.float()), ref.features, 1e-2, "U-Net output")
+
+
+def test_config5_kernel_map(cuda):
+    wl = syn.config5(64)
+    y, seen = _run(wl, cuda, torch.float16)
+    _check_digests("config5", wl, seen)
+
+
+@pytest.mark.parametrize("channels", [64, 128, 256])
+def test_config5_features_rows(cuda, channels):
+    """Full batch of 16 x 500k voxels on the GPU; the oracle recomputes a
+    random 20k-row subset of the outputs from the oracle's own pairs."""
+    wl = syn.config5(channels)
+    y, seen = _run(wl, cuda, torch.float16)
+    rng = np.random.default_rng(channels)
+    rows = np.sort(rng.choice(wl.n_voxels, 20000, replace=False))
+    spec = wl.layers[0]
+    pairs = oracle.subm_pairs(wl.indices, wl.spatial_shape, wl.batch_size, 3)
+    w = oracle.normalize_weight(spec["weight"].astype(np.float32), (3, 3, 3), channels, channels)
+    want = np.zeros((len(rows), channels), np.float32)
+    pos = np.full(wl.n_voxels, -1, np.int64)
+    pos[rows] = np.arange(len(rows))
+    f = wl.features.astype(np.float32)
+    for k in range(27):
+        sel = pos[pairs.pairs_out[k]] >= 0
+        if sel.any():
+            want[pos[pairs.pairs_out[k][sel]]] += f[pairs.pairs_in[k][sel]] @ w[k]
+    got = np_(y.features[torch.from_numpy(rows).to(cuda)].float())
+    assert_close_rel(got, want, 1e-2, f"config5 C={channels}")

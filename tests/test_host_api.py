@@ -1,0 +1,161 @@
+"""Host-side behaviour of the drop-in API (no GPU): constructors, errors,
+weight layout, SparseConvTensor container semantics.  Mirrors the
+reference's tests/test_tensor.py and the ctor checks of modules.py:46-51."""
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+import trispconv_b200.pytorch as spconv
+from trispconv_b200.pytorch.indices import IndiceData, _output_spatial_shape, _to3
+from trispconv_b200.pytorch.weight import normalize_spconv_weight
+from trispconv_b200.testing.synthetic import generate_sparse_data, sparse_data_to_tensors
+
+
+def make_sparse(B=1, N=8, C=4, D=8, H=8, W=8):
+    coords = torch.randint(0, min(D, H, W), (N, 3), dtype=torch.int32)
+    indices = torch.cat([torch.zeros(N, 1, dtype=torch.int32), coords], dim=1)
+    return spconv.SparseConvTensor(torch.randn(N, C), indices, [D, H, W], B)
+
+
+def test_exports():
+    for name in ["SparseConvTensor", "SparseConvolution", "SubMConv3d", "SparseConv3d",
+                 "SparseInverseConv3d", "SparseSequential", "SparseModule", "ConvAlgo"]:
+        assert hasattr(spconv, name)
+    assert [a.name for a in spconv.ConvAlgo] == ["Native", "MaskImplicitGemm", "MaskSplitImplicitGemm"]
+
+
+def test_tensor_construction_and_replace():
+    x = make_sparse()
+    assert x.features.shape == (8, 4) and x.indices.shape == (8, 4)
+    assert x.spatial_shape == [8, 8, 8] and x.batch_size == 1
+    y = x.replace_feature(torch.ones(8, 4))
+    assert y.indices is x.indices and y.indice_dict is x.indice_dict
+    assert not torch.equal(x.features, y.features)
+    with pytest.raises(AttributeError):
+        x.features = torch.zeros(8, 4)
+    assert x.find_indice_pair(None) is None and x.find_indice_pair("nope") is None
+
+
+def test_tensor_asserts_int32():
+    with pytest.raises(AssertionError):
+        spconv.SparseConvTensor(torch.randn(3, 2), torch.zeros(3, 4, dtype=torch.int64), [4, 4, 4], 1)
+    with pytest.raises(AssertionError):
+        spconv.SparseConvTensor(torch.randn(3), torch.zeros(3, 4, dtype=torch.int32), [4, 4, 4], 1)
+
+
+def test_dense_host_tensor():
+    x = make_sparse(B=2, N=10, C=3, D=4, H=5, W=6)
+    idx = x.indices.clone()
+    idx[:, 1] %= 4
+    idx[:5, 0] = 0
+    idx[5:, 0] = 1
+    x2 = spconv.SparseConvTensor(x.features, idx, [4, 5, 6], 2)
+    d = x2.dense()
+    assert d.shape == (2, 3, 4, 5, 6)
+    assert x2.dense(channels_first=False).shape == (2, 4, 5, 6, 3)
+    bad = idx.clone()
+    bad[0, 1] = 9
+    with pytest.raises(AssertionError):
+        spconv.SparseConvTensor(x.features, bad, [4, 5, 6], 2).dense()
+
+
+def test_ctor_errors():
+    with pytest.raises(NotImplementedError):
+        spconv.SparseConvolution(2, 4, 4, 3)
+    with pytest.raises(NotImplementedError):
+        spconv.SparseConvolution(3, 4, 4, 3, groups=2)
+    with pytest.raises(NotImplementedError):
+        spconv.SparseConvolution(3, 4, 4, 3, transposed=True)
+    spconv.SparseConvolution(3, 4, 4, 3, transposed=True, inverse=True)
+
+
+def test_module_parameters_krsc():
+    m = spconv.SubMConv3d(4, 8, 3, stride=2, padding=1, indice_key="k", algo=spconv.ConvAlgo.Native)
+    assert m.weight.shape == (8, 3, 3, 3, 4) and m.bias.shape == (8,)
+    assert m.stride == (1, 1, 1) and m.padding == (0, 0, 0)
+    s = spconv.SparseConv3d(4, 8, (3, 1, 1), stride=(2, 1, 1), bias=False)
+    assert s.weight.shape == (8, 3, 1, 1, 4) and s.bias is None
+    assert set(s.state_dict()) == {"weight"}
+    inv = spconv.SparseInverseConv3d(8, 4, 3, indice_key="k")
+    assert inv.inverse and not inv.subm
+    # kaiming-uniform bound sqrt(6 / fan_in)
+    bound = np.sqrt(6.0 / (27 * 4))
+    assert float(m.weight.abs().max()) <= bound + 1e-6
+
+
+def test_weight_normalizer():
+    w = torch.randn(8, 3, 3, 3, 4)
+    n = normalize_spconv_weight(w, (3, 3, 3), 4, 8)
+    assert n.shape == (27, 4, 8)
+    assert torch.equal(n, w.reshape(8, 27, 4).permute(1, 2, 0))
+    w1 = torch.randn(6, 1, 1, 1, 5)
+    n1 = normalize_spconv_weight(w1, (1, 1, 1), 5, 6)
+    assert torch.equal(n1[0], w1.reshape(30).view(5, 6))  # spconv 1x1x1 quirk
+    assert torch.equal(normalize_spconv_weight(w1.reshape(6, 5), (1, 1, 1), 5, 6), n1)
+    assert normalize_spconv_weight(n, (3, 3, 3), 4, 8) is not None
+    with pytest.raises(ValueError):
+        normalize_spconv_weight(torch.randn(2, 2), (3, 3, 3), 4, 8)
+
+
+def test_kernel_weight_views_match_normalizer():
+    """The conv kernel reads the KRSC parameter in place; check that the
+    layouts it is handed address exactly normalize_spconv_weight's values."""
+    for ks in [(3, 3, 3), (1, 1, 1), (3, 1, 1), (2, 2, 2)]:
+        m = spconv.SparseConv3d(5, 7, ks)
+        K = int(np.prod(ks))
+        w, layout = m._kernel_weight(K)
+        ref = m._get_weight()
+        if layout == 1:  # KRSC (Cout, K, Cin): element (k, c, n) = w[n, k, c]
+            got = w.reshape(7, K, 5).permute(1, 2, 0)
+        else:
+            got = w.reshape(K, 5, 7)
+        assert torch.equal(got, ref), ks
+    m = spconv.SparseInverseConv3d(5, 7, 3)
+    w, layout = m._kernel_weight(1)
+    assert layout == 0 and torch.equal(w, m._get_weight()[:1])
+    with pytest.raises(IndexError):
+        spconv.SubMConv3d(5, 7, 1)._kernel_weight(27)
+
+
+def test_helpers():
+    assert _to3(3) == (3, 3, 3) and _to3([1, 2, 3]) == (1, 2, 3)
+    assert _output_spatial_shape((8, 8, 8), (3, 3, 3), (2, 2, 2), (1, 1, 1), (1, 1, 1)) == (4, 4, 4)
+    assert _output_spatial_shape((41, 1600, 1408), (3, 3, 3), (2, 2, 2), (1, 1, 1), (1, 1, 1)) == (21, 800, 704)
+
+
+def test_indice_data_fields():
+    d = IndiceData(torch.zeros(0, 4, dtype=torch.int32), [torch.zeros(0, dtype=torch.long)],
+                   [torch.zeros(0, dtype=torch.long)], torch.zeros(1, dtype=torch.long),
+                   torch.zeros(0, 4, dtype=torch.int32), (4, 4, 4), (4, 4, 4), (1, 1, 1), (1, 1, 1),
+                   (0, 0, 0), (1, 1, 1), True)
+    assert d.subm and d.kernel_size == (1, 1, 1) and len(d.pairs_in) == 1 and d.pair_num.shape == (1,)
+
+
+def test_host_tensors_rejected():
+    """No CPU fallback: the conv path refuses host tensors loudly."""
+    x = make_sparse(C=4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        spconv.SubMConv3d(4, 4, 3)(x)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        spconv.SparseSequential(spconv.SparseConv3d(4, 4, 3, stride=2), nn.ReLU())(x)
+
+
+def test_generate_sparse_data_roundtrip():
+    d = generate_sparse_data([5, 6, 7], [20, 30], 3, seed=1)
+    f, dense, idx = sparse_data_to_tensors(d)
+    assert idx.dtype == torch.int32 and idx.shape == (50, 4)
+    assert torch.equal(dense[idx[:, 0].long(), :, idx[:, 1].long(), idx[:, 2].long(), idx[:, 3].long()], f)
+    for b in range(2):
+        sel = idx[idx[:, 0] == b]
+        assert len(torch.unique(sel, dim=0)) == len(sel)
+
+
+def test_sequential_dict_and_kwargs():
+    seq = spconv.SparseSequential({"a": nn.ReLU(), "b": nn.Identity()})
+    assert list(dict(seq.named_children())) == ["a", "b"]
+    seq2 = spconv.SparseSequential(nn.ReLU(), extra=nn.Identity())
+    assert list(dict(seq2.named_children())) == ["0", "extra"]
+    x = make_sparse()
+    y = spconv.SparseSequential(nn.ReLU())(x)
+    assert (y.features >= 0).all() and y.indices is x.indices

@@ -1,0 +1,930 @@
+// Kernel-map (indice-pair) generation on the GPU.
+//
+// Reference behaviour being replaced (mrpulford/trispconv):
+//   trispconv/pytorch/indices.py:54-64    dense B*D*H*W int64 lookup table
+//   trispconv/pytorch/indices.py:67-140   submanifold pairs, offset loop kz,ky,kx
+//   trispconv/pytorch/indices.py:143-259  strided pairs, torch.unique(sorted=True)
+//   trispconv/pytorch/modules.py:175-213  inverse pairs (participation + swap)
+//
+// Design (B200): the dense table becomes an open-addressing hash of packed
+// 64-bit entries (cell key << 32 | row) built with atomicCAS; the strided
+// output set becomes a 1-bit-per-cell occupancy bitmap whose prefix popcount
+// gives every output cell its rank in sorted key order.  All maps are k-major
+// int32 arrays so that per-offset reads and writes are coalesced.
+#include <cstdint>
+
+#include "tsc_common.cuh"
+
+namespace tsc {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kItems = 8;                          // words / flags per thread in scans
+constexpr int kTile = kThreads * kItems;           // 2048 per block
+constexpr int kScanBlockThreads = 1024;
+constexpr uint64_t kMaxCells = 0xFFFFFFFEull;      // keys must stay below the empty sentinel
+
+struct GeoDev {
+  int B, D, H, W;
+  int oD, oH, oW;
+  int kD, kH, kW;
+  int sz, sy, sx;
+  int pz, py, px;
+  int dz, dy, dx;
+};
+
+GeoDev to_dev(const tsc_geometry& g) {
+  GeoDev d;
+  d.B = g.batch;
+  d.D = g.in_shape[0]; d.H = g.in_shape[1]; d.W = g.in_shape[2];
+  d.oD = g.out_shape[0]; d.oH = g.out_shape[1]; d.oW = g.out_shape[2];
+  d.kD = g.ksize[0]; d.kH = g.ksize[1]; d.kW = g.ksize[2];
+  d.sz = g.stride[0]; d.sy = g.stride[1]; d.sx = g.stride[2];
+  d.pz = g.padding[0]; d.py = g.padding[1]; d.px = g.padding[2];
+  d.dz = g.dilation[0]; d.dy = g.dilation[1]; d.dx = g.dilation[2];
+  return d;
+}
+
+int log2_ceil(uint64_t v) {
+  int l = 0;
+  while ((1ull << l) < v) ++l;
+  return l;
+}
+
+// Capacity of the submanifold hash: load factor <= 1/2.
+int subm_log2cap(int64_t n) {
+  int l = log2_ceil(static_cast<uint64_t>(n < 1 ? 1 : n) * 2);
+  return l < 8 ? 8 : l;
+}
+
+__device__ __forceinline__ bool in_grid(const int4& c, int B, int D, int H, int W) {
+  return static_cast<unsigned>(c.x) < static_cast<unsigned>(B) &&
+         static_cast<unsigned>(c.y) < static_cast<unsigned>(D) &&
+         static_cast<unsigned>(c.z) < static_cast<unsigned>(H) &&
+         static_cast<unsigned>(c.w) < static_cast<unsigned>(W);
+}
+
+// Linear cell key b*DHW + z*HW + y*W + x (indices.py:45-51).  The host checks
+// B*D*H*W <= kMaxCells, so every partial product fits in 32 bits.
+__device__ __forceinline__ uint32_t cell_key(unsigned b, unsigned z, unsigned y, unsigned x,
+                                             unsigned D, unsigned H, unsigned W) {
+  return ((b * D + z) * H + y) * W + x;
+}
+
+// ---------------------------------------------------------------------------
+// Submanifold: hash build + per-offset query
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kThreads)
+k_hash_build(const int4* __restrict__ idx, int64_t n, int B, int D, int H, int W,
+             unsigned long long* __restrict__ table, int log2cap, int64_t* __restrict__ status) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int4 c = idx[i];
+  if (!in_grid(c, B, D, H, W)) {
+    raise_status(status, TSC_STATUS_KEY_RANGE);
+    return;
+  }
+  const uint32_t key = cell_key(c.x, c.y, c.z, c.w, D, H, W);
+  const unsigned long long entry = (static_cast<unsigned long long>(key) << 32) |
+                                   static_cast<uint32_t>(i);
+  const uint32_t mask = (1u << log2cap) - 1u;
+  uint32_t slot = hash_slot(key, log2cap);
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    unsigned long long cur = table[slot];
+    if (cur == kEmptySlot) {
+      cur = atomicCAS(&table[slot], kEmptySlot, entry);
+      if (cur == kEmptySlot) return;
+    }
+    if (static_cast<uint32_t>(cur >> 32) == key) {
+      // Duplicate coordinate: the highest row wins, like the reference's
+      // in-order `table[encoded] = arange(N)` (indices.py:63).
+      atomicMax(&table[slot], entry);
+      return;
+    }
+    slot = (slot + 1u) & mask;
+  }
+  raise_status(status, TSC_STATUS_HASH_FULL);
+}
+
+__device__ __forceinline__ int hash_lookup(const unsigned long long* __restrict__ table,
+                                           int log2cap, uint32_t key) {
+  const uint32_t mask = (1u << log2cap) - 1u;
+  uint32_t slot = hash_slot(key, log2cap);
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    const unsigned long long e = __ldg(&table[slot]);
+    if (e == kEmptySlot) return -1;
+    if (static_cast<uint32_t>(e >> 32) == key) return static_cast<int>(static_cast<uint32_t>(e));
+    slot = (slot + 1u) & mask;
+  }
+  return -1;
+}
+
+// One thread per (offset k = blockIdx.y, row i).  Writes gather_map[k][i] and
+// accumulates pair_num[k].  Offsets follow indices.py:96-98:
+// (k_dim - K_dim//2) * dilation.
+__global__ void __launch_bounds__(kThreads)
+k_subm_query(const int4* __restrict__ idx, int64_t n, GeoDev g,
+             const unsigned long long* __restrict__ table, int log2cap,
+             int32_t* __restrict__ gmap, unsigned long long* __restrict__ meta) {
+  const int k = blockIdx.y;
+  const KOffset ko = split_k(k, g.kH, g.kW);
+  const int offz = (ko.kz - g.kD / 2) * g.dz;
+  const int offy = (ko.ky - g.kH / 2) * g.dy;
+  const int offx = (ko.kx - g.kW / 2) * g.dx;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  int found = -1;
+  if (i < n) {
+    const int4 c = __ldg(&idx[i]);
+    const int nz = c.y + offz, ny = c.z + offy, nx = c.w + offx;
+    if (static_cast<unsigned>(c.x) < static_cast<unsigned>(g.B) &&
+        static_cast<unsigned>(nz) < static_cast<unsigned>(g.D) &&
+        static_cast<unsigned>(ny) < static_cast<unsigned>(g.H) &&
+        static_cast<unsigned>(nx) < static_cast<unsigned>(g.W)) {
+      found = hash_lookup(table, log2cap, cell_key(c.x, nz, ny, nx, g.D, g.H, g.W));
+    }
+    gmap[static_cast<int64_t>(k) * n + i] = found;
+  }
+  const int cnt = __syncthreads_count(found >= 0);
+  if (threadIdx.x == 0 && cnt) atomicAdd(&meta[TSC_META_COUNTS + k], static_cast<unsigned long long>(cnt));
+}
+
+// ---------------------------------------------------------------------------
+// Strided: occupancy bitmap over the output grid
+// ---------------------------------------------------------------------------
+
+// Per input row, walks the K offsets in reference order (indices.py:177-187):
+// c = i + p - k*d is a valid output position iff c >= 0, c % s == 0 and
+// c / s < out (for c >= 0 C and Python division agree).
+__global__ void __launch_bounds__(kThreads)
+k_strided_mark(const int4* __restrict__ idx, int64_t n, GeoDev g, uint32_t* __restrict__ bitmap,
+               unsigned long long* __restrict__ meta, int64_t* __restrict__ status) {
+  extern __shared__ unsigned int s_cnt[];  // K pair counters + 1 participation counter
+  const int K = g.kD * g.kH * g.kW;
+  for (int t = threadIdx.x; t <= K; t += blockDim.x) s_cnt[t] = 0u;
+  __syncthreads();
+
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  bool active = i < n;
+  int4 c = make_int4(0, 0, 0, 0);
+  if (active) {
+    c = __ldg(&idx[i]);
+    if (!in_grid(c, g.B, g.D, g.H, g.W)) {
+      raise_status(status, TSC_STATUS_KEY_RANGE);
+      active = false;
+    }
+  }
+  const int lane = threadIdx.x & 31;
+  bool any = false;
+  int k = 0;
+  for (int kz = 0; kz < g.kD; ++kz) {
+    const int cz = c.y + g.pz - kz * g.dz;
+    const bool vz = cz >= 0 && (cz % g.sz) == 0 && (cz / g.sz) < g.oD;
+    const int oz = vz ? cz / g.sz : 0;
+    for (int ky = 0; ky < g.kH; ++ky) {
+      const int cy = c.z + g.py - ky * g.dy;
+      const bool vy = vz && cy >= 0 && (cy % g.sy) == 0 && (cy / g.sy) < g.oH;
+      const int oy = vy ? cy / g.sy : 0;
+      for (int kx = 0; kx < g.kW; ++kx, ++k) {
+        const int cx = c.w + g.px - kx * g.dx;
+        const bool v = active && vy && cx >= 0 && (cx % g.sx) == 0 && (cx / g.sx) < g.oW;
+        if (v) {
+          const uint32_t lin = cell_key(c.x, oz, oy, cx / g.sx, g.oD, g.oH, g.oW);
+          atomicOr(&bitmap[lin >> 5], 1u << (lin & 31u));
+          any = true;
+        }
+        const unsigned b = __ballot_sync(kFullMask, v);
+        if (lane == 0 && b) atomicAdd(&s_cnt[k], static_cast<unsigned>(__popc(b)));
+      }
+    }
+  }
+  const unsigned b = __ballot_sync(kFullMask, any);
+  if (lane == 0 && b) atomicAdd(&s_cnt[K], static_cast<unsigned>(__popc(b)));
+  __syncthreads();
+  for (int t = threadIdx.x; t < K; t += blockDim.x)
+    if (s_cnt[t]) atomicAdd(&meta[TSC_META_COUNTS + t], static_cast<unsigned long long>(s_cnt[t]));
+  if (threadIdx.x == 0 && s_cnt[K])
+    atomicAdd(&meta[TSC_META_N_PART], static_cast<unsigned long long>(s_cnt[K]));
+}
+
+// Popcount of each 2048-word tile of the (zero-padded) bitmap.
+__global__ void __launch_bounds__(kThreads)
+k_bitmap_tile_count(const uint4* __restrict__ bitmap, uint32_t* __restrict__ block_sums) {
+  __shared__ uint32_t ws[32];
+  const size_t q = (static_cast<size_t>(blockIdx.x) * kTile + threadIdx.x * kItems) / 4;
+  const uint4 a = bitmap[q], b = bitmap[q + 1];
+  const uint32_t s = __popc(a.x) + __popc(a.y) + __popc(a.z) + __popc(a.w) + __popc(b.x) +
+                     __popc(b.y) + __popc(b.z) + __popc(b.w);
+  uint32_t total;
+  block_exclusive_scan(s, ws, &total);
+  if (threadIdx.x == 0) block_sums[blockIdx.x] = total;
+}
+
+// Single-block exclusive scan of per-tile sums, in place; sums[nblocks] gets the
+// total.  Optionally publishes the total and a status snapshot into meta.
+template <typename U>
+__global__ void __launch_bounds__(kScanBlockThreads)
+k_scan_tile_sums(U* __restrict__ sums, int64_t nblocks, unsigned long long* __restrict__ meta,
+                 int meta_slot, const int64_t* __restrict__ status) {
+  __shared__ U ws[32];
+  U carry = 0;
+  for (int64_t base = 0; base < nblocks; base += blockDim.x) {
+    const int64_t t = base + threadIdx.x;
+    const U v = t < nblocks ? sums[t] : U(0);
+    U tot;
+    U ex;
+    if constexpr (sizeof(U) == 8) {
+      ex = block_exclusive_scan64(v, reinterpret_cast<unsigned long long*>(ws),
+                                  reinterpret_cast<unsigned long long*>(&tot));
+    } else {
+      ex = block_exclusive_scan(v, reinterpret_cast<uint32_t*>(ws), reinterpret_cast<uint32_t*>(&tot));
+    }
+    if (t < nblocks) sums[t] = carry + ex;
+    carry += tot;
+  }
+  if (threadIdx.x == 0) {
+    sums[nblocks] = carry;
+    if (meta != nullptr) {
+      meta[meta_slot] = static_cast<unsigned long long>(carry);
+      if (status != nullptr) meta[TSC_META_STATUS] = static_cast<unsigned long long>(*status);
+    }
+  }
+}
+
+// Writes the exclusive prefix popcount of every bitmap word and the sorted
+// output coordinates (rank order == ascending cell key == the reference's
+// unique(sorted=True) order, decoded as indices.py:223-229).
+__global__ void __launch_bounds__(kThreads)
+k_bitmap_emit(const uint4* __restrict__ bitmap, const uint32_t* __restrict__ tile_off,
+              uint32_t* __restrict__ word_prefix, GeoDev g, int4* __restrict__ out_idx, int64_t n_out) {
+  __shared__ uint32_t ws[32];
+  const size_t w0 = static_cast<size_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
+  const uint4 a = bitmap[w0 / 4], b = bitmap[w0 / 4 + 1];
+  const uint32_t words[kItems] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) s += __popc(words[j]);
+  uint32_t total;
+  uint32_t ex = block_exclusive_scan(s, ws, &total) + tile_off[blockIdx.x];
+  uint32_t pre[kItems];
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    pre[j] = ex;
+    ex += __popc(words[j]);
+  }
+  uint4* wp = reinterpret_cast<uint4*>(word_prefix + w0);
+  wp[0] = make_uint4(pre[0], pre[1], pre[2], pre[3]);
+  wp[1] = make_uint4(pre[4], pre[5], pre[6], pre[7]);
+  const unsigned oW = g.oW, oH = g.oH, oD = g.oD;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    uint32_t wv = words[j];
+    uint32_t r = pre[j];
+    while (wv) {
+      const int bit = __ffs(wv) - 1;
+      wv &= wv - 1u;
+      const uint32_t lin = static_cast<uint32_t>((w0 + j) * 32u + bit);
+      const uint32_t x = lin % oW;
+      uint32_t t = lin / oW;
+      const uint32_t y = t % oH;
+      t /= oH;
+      const uint32_t z = t % oD;
+      const uint32_t bb = t / oD;
+      if (r < n_out)
+        out_idx[r] = make_int4(static_cast<int>(bb), static_cast<int>(z), static_cast<int>(y),
+                               static_cast<int>(x));
+      ++r;
+    }
+  }
+}
+
+__device__ __forceinline__ void push_overflow(int32_t* overflow, int64_t cap,
+                                              unsigned long long* meta, int64_t* status, int k,
+                                              int o, int i) {
+  const unsigned long long slot = atomicAdd(&meta[TSC_META_N_OVERFLOW], 1ull);
+  if (static_cast<int64_t>(slot) < cap) {
+    overflow[3 * slot + 0] = k;
+    overflow[3 * slot + 1] = o;
+    overflow[3 * slot + 2] = i;
+  } else {
+    raise_status(status, TSC_STATUS_OVERFLOW_FULL);
+  }
+}
+
+// Per input row and offset: rank of the output cell, written to the
+// input-stationary scatter map and (first writer wins) to the
+// output-stationary gather map.  A second input row for the same (k, o) can
+// only come from duplicate input coordinates; it goes to the overflow list.
+__global__ void __launch_bounds__(kThreads)
+k_strided_pairs(const int4* __restrict__ idx, int64_t n, GeoDev g,
+                const uint32_t* __restrict__ bitmap, const uint32_t* __restrict__ word_prefix,
+                int64_t n_out, int32_t* __restrict__ gmap, int32_t* __restrict__ smap,
+                int32_t* __restrict__ overflow, int64_t ovf_cap,
+                unsigned long long* __restrict__ meta, int64_t* __restrict__ status) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int4 c = __ldg(&idx[i]);
+  const bool active = in_grid(c, g.B, g.D, g.H, g.W);
+  int k = 0;
+  for (int kz = 0; kz < g.kD; ++kz) {
+    const int cz = c.y + g.pz - kz * g.dz;
+    const bool vz = active && cz >= 0 && (cz % g.sz) == 0 && (cz / g.sz) < g.oD;
+    const int oz = vz ? cz / g.sz : 0;
+    for (int ky = 0; ky < g.kH; ++ky) {
+      const int cy = c.z + g.py - ky * g.dy;
+      const bool vy = vz && cy >= 0 && (cy % g.sy) == 0 && (cy / g.sy) < g.oH;
+      const int oy = vy ? cy / g.sy : 0;
+      for (int kx = 0; kx < g.kW; ++kx, ++k) {
+        const int cx = c.w + g.px - kx * g.dx;
+        const bool v = vy && cx >= 0 && (cx % g.sx) == 0 && (cx / g.sx) < g.oW;
+        int o = -1;
+        if (v) {
+          const uint32_t lin = cell_key(c.x, oz, oy, cx / g.sx, g.oD, g.oH, g.oW);
+          const uint32_t w = lin >> 5;
+          o = static_cast<int>(__ldg(&word_prefix[w]) +
+                               __popc(__ldg(&bitmap[w]) & ((1u << (lin & 31u)) - 1u)));
+          if (o >= n_out) {
+            raise_status(status, TSC_STATUS_KEY_RANGE);
+            smap[static_cast<int64_t>(k) * n + i] = -1;
+            continue;
+          }
+          const int prev = atomicCAS(&gmap[static_cast<int64_t>(k) * n_out + o], -1,
+                                     static_cast<int>(i));
+          if (prev != -1) push_overflow(overflow, ovf_cap, meta, status, k, o, static_cast<int>(i));
+        }
+        smap[static_cast<int64_t>(k) * n + i] = o;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Row compaction (inverse convs): flags -> exclusive prefix
+// ---------------------------------------------------------------------------
+
+// Participation of input row i in a k-major map: any map[k][i] >= 0.
+__device__ __forceinline__ bool row_participates(const int32_t* __restrict__ map, int K, int64_t n,
+                                                 int64_t i) {
+  for (int k = 0; k < K; ++k)
+    if (__ldg(&map[static_cast<int64_t>(k) * n + i]) >= 0) return true;
+  return false;
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_part_tile_count(const int32_t* __restrict__ map, int K, int64_t n, uint32_t* __restrict__ block_sums) {
+  __shared__ uint32_t ws[32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int64_t i = base + j;
+    if (i < n && row_participates(map, K, n, i)) ++s;
+  }
+  uint32_t total;
+  block_exclusive_scan(s, ws, &total);
+  if (threadIdx.x == 0) block_sums[blockIdx.x] = total;
+}
+
+// For participating rows (ascending): compact[i] = r, out_idx[r] = in_idx[i],
+// inv_gather[k][r] = smap[k][i].
+__global__ void __launch_bounds__(kThreads)
+k_inverse_strided_emit(const int4* __restrict__ in_idx, const int32_t* __restrict__ smap, int K,
+                       int64_t n, const uint32_t* __restrict__ tile_off, int64_t n_part,
+                       int4* __restrict__ out_idx, int32_t* __restrict__ inv_gather,
+                       int32_t* __restrict__ compact) {
+  __shared__ uint32_t ws[32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
+  bool flag[kItems];
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int64_t i = base + j;
+    flag[j] = i < n && row_participates(smap, K, n, i);
+    s += flag[j] ? 1u : 0u;
+  }
+  uint32_t total;
+  uint32_t r = block_exclusive_scan(s, ws, &total) + tile_off[blockIdx.x];
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int64_t i = base + j;
+    if (i >= n) break;
+    if (compact != nullptr) compact[i] = flag[j] ? static_cast<int32_t>(r) : -1;
+    if (flag[j] && r < n_part) {
+      out_idx[r] = in_idx[i];
+      for (int k = 0; k < K; ++k)
+        inv_gather[static_cast<int64_t>(k) * n_part + r] = smap[static_cast<int64_t>(k) * n + i];
+      ++r;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_iota(int32_t* __restrict__ out, int64_t n) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = static_cast<int32_t>(i);
+}
+
+// Inverse of a submanifold map: flag every row j read by some pair.
+__global__ void __launch_bounds__(kThreads)
+k_flag_targets(const int32_t* __restrict__ gmap, int64_t total, int64_t n, int32_t* __restrict__ flags) {
+  const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= total) return;
+  const int j = gmap[e];
+  if (j >= 0 && j < n) flags[j] = 1;
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_flag_tile_count(const int32_t* __restrict__ flags, int64_t n, uint32_t* __restrict__ block_sums) {
+  __shared__ uint32_t ws[32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int64_t i = base + j;
+    if (i < n && flags[i] != 0) ++s;
+  }
+  uint32_t total;
+  block_exclusive_scan(s, ws, &total);
+  if (threadIdx.x == 0) block_sums[blockIdx.x] = total;
+}
+
+// flags (0/1) -> compact ids (r or -1), in place.
+__global__ void __launch_bounds__(kThreads)
+k_flag_compact(int32_t* __restrict__ flags, int64_t n, const uint32_t* __restrict__ tile_off) {
+  __shared__ uint32_t ws[32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
+  int32_t f[kItems];
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int64_t i = base + j;
+    f[j] = (i < n) ? flags[i] : 0;
+    s += f[j] != 0 ? 1u : 0u;
+  }
+  uint32_t total;
+  uint32_t r = block_exclusive_scan(s, ws, &total) + tile_off[blockIdx.x];
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int64_t i = base + j;
+    if (i < n) {
+      flags[i] = f[j] != 0 ? static_cast<int32_t>(r) : -1;
+      if (f[j] != 0) ++r;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_gather_rows(const int4* __restrict__ in_idx, const int32_t* __restrict__ compact, int64_t n,
+              int64_t n_part, int4* __restrict__ out_idx) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int r = compact[i];
+  if (r >= 0 && r < n_part) out_idx[r] = in_idx[i];
+}
+
+// inv_gather[k][compact[j]] = i for gather_map[k][i] = j.
+__global__ void __launch_bounds__(kThreads)
+k_transpose_map(const int32_t* __restrict__ gmap, int K, int64_t n, const int32_t* __restrict__ compact,
+                int64_t n_part, int32_t* __restrict__ inv_gather, int32_t* __restrict__ overflow,
+                int64_t ovf_cap, unsigned long long* __restrict__ meta, int64_t* __restrict__ status) {
+  const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= static_cast<int64_t>(K) * n) return;
+  const int j = gmap[e];
+  if (j < 0 || j >= n) return;
+  const int k = static_cast<int>(e / n);
+  const int i = static_cast<int>(e - static_cast<int64_t>(k) * n);
+  const int r = compact[j];
+  if (r < 0 || r >= n_part) return;
+  const int prev = atomicCAS(&inv_gather[static_cast<int64_t>(k) * n_part + r], -1, i);
+  if (prev != -1) push_overflow(overflow, ovf_cap, meta, status, k, r, i);
+}
+
+// ---------------------------------------------------------------------------
+// Pair-list materialisation (k-major scan over a [K][n] map)
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kThreads)
+k_map_tile_count(const int32_t* __restrict__ map, int64_t total, unsigned long long* __restrict__ block_sums) {
+  __shared__ uint32_t ws[32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int64_t e = base + j;
+    if (e < total && map[e] >= 0) ++s;
+  }
+  uint32_t t;
+  block_exclusive_scan(s, ws, &t);
+  if (threadIdx.x == 0) block_sums[blockIdx.x] = t;
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_map_emit_pairs(const int32_t* __restrict__ map, int64_t total, int64_t n, int mode,
+                 const int32_t* __restrict__ remap, const unsigned long long* __restrict__ tile_off,
+                 int64_t* __restrict__ pairs_in, int64_t* __restrict__ pairs_out, int64_t capacity) {
+  __shared__ uint32_t ws[32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
+  int32_t v[kItems];
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    const int64_t e = base + j;
+    v[j] = e < total ? map[e] : -1;
+    s += v[j] >= 0 ? 1u : 0u;
+  }
+  uint32_t t;
+  unsigned long long pos = block_exclusive_scan(s, ws, &t) + tile_off[blockIdx.x];
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    if (v[j] < 0) continue;
+    if (static_cast<int64_t>(pos) >= capacity) break;
+    const int64_t e = base + j;
+    const int64_t k = e / n;
+    const int64_t idx = e - k * n;
+    if (mode == 0) {
+      pairs_in[pos] = v[j];
+      pairs_out[pos] = idx;
+    } else {
+      pairs_in[pos] = idx;
+      pairs_out[pos] = remap != nullptr ? static_cast<int64_t>(remap[v[j]]) : static_cast<int64_t>(v[j]);
+    }
+    ++pos;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_pairs_to_gather(const int64_t* __restrict__ pin, const int64_t* __restrict__ pout, int64_t count,
+                  int k, int64_t n_out, int32_t* __restrict__ gmap, int32_t* __restrict__ overflow,
+                  int64_t ovf_cap, unsigned long long* __restrict__ meta, int64_t* __restrict__ status) {
+  const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (p >= count) return;
+  const int64_t o = pout[p];
+  const int64_t i = pin[p];
+  if (o < 0 || o >= n_out || i < 0 || i > 0x7fffffffLL) {
+    raise_status(status, TSC_STATUS_KEY_RANGE);
+    return;
+  }
+  const int prev = atomicCAS(&gmap[static_cast<int64_t>(k) * n_out + o], -1, static_cast<int>(i));
+  if (prev != -1) push_overflow(overflow, ovf_cap, meta, status, k, static_cast<int>(o), static_cast<int>(i));
+}
+
+// ---------------------------------------------------------------------------
+// Host-side validation helpers
+// ---------------------------------------------------------------------------
+
+int check_shape3(const int32_t* s, const char* what) {
+  for (int d = 0; d < 3; ++d) {
+    if (s[d] <= 0) {
+      set_error("%s[%d] = %d must be positive", what, d, s[d]);
+      return TSC_ERR_INVALID_ARG;
+    }
+  }
+  return TSC_OK;
+}
+
+int check_geometry(const tsc_geometry* geo, bool strided) {
+  TSC_CHECK_ARG(geo != nullptr, "geometry is NULL");
+  TSC_CHECK_ARG(geo->batch > 0, "batch_size must be positive, got %d", geo->batch);
+  int rc;
+  if ((rc = check_shape3(geo->in_shape, "spatial_shape")) != TSC_OK) return rc;
+  if ((rc = check_shape3(geo->ksize, "kernel_size")) != TSC_OK) return rc;
+  if ((rc = check_shape3(geo->dilation, "dilation")) != TSC_OK) return rc;
+  if (strided) {
+    if ((rc = check_shape3(geo->out_shape, "output spatial_shape")) != TSC_OK) return rc;
+    if ((rc = check_shape3(geo->stride, "stride")) != TSC_OK) return rc;
+    for (int d = 0; d < 3; ++d)
+      TSC_CHECK_ARG(geo->padding[d] >= 0, "padding[%d] = %d must be >= 0", d, geo->padding[d]);
+  }
+  const int64_t K = static_cast<int64_t>(geo->ksize[0]) * geo->ksize[1] * geo->ksize[2];
+  TSC_CHECK_ARG(K <= 4096, "kernel volume %lld exceeds 4096", static_cast<long long>(K));
+  return TSC_OK;
+}
+
+uint64_t cells_of(int32_t batch, const int32_t* s) {
+  return static_cast<uint64_t>(batch) * static_cast<uint64_t>(s[0]) * static_cast<uint64_t>(s[1]) *
+         static_cast<uint64_t>(s[2]);
+}
+
+struct StridedWs {
+  uint64_t nbits;
+  int64_t nwords_pad;
+  int64_t nblocks;
+  size_t off_prefix, off_sums, bytes;
+};
+
+StridedWs strided_ws(const tsc_geometry& g) {
+  StridedWs w;
+  w.nbits = cells_of(g.batch, g.out_shape);
+  const int64_t nwords = static_cast<int64_t>((w.nbits + 31) / 32);
+  w.nblocks = ceil_div(nwords < 1 ? 1 : nwords, kTile);
+  w.nwords_pad = w.nblocks * kTile;
+  w.off_prefix = align_up(static_cast<size_t>(w.nwords_pad) * 4, 256);
+  w.off_sums = w.off_prefix + align_up(static_cast<size_t>(w.nwords_pad) * 4, 256);
+  w.bytes = w.off_sums + align_up(static_cast<size_t>(w.nblocks + 1) * 4, 256);
+  return w;
+}
+
+size_t rows_scan_bytes(int64_t n) {
+  const int64_t nblocks = ceil_div(n < 1 ? 1 : n, kTile);
+  return align_up(static_cast<size_t>(nblocks + 1) * 8, 256);
+}
+
+}  // namespace
+}  // namespace tsc
+
+using namespace tsc;
+
+extern "C" {
+
+size_t tsc_subm_kmap_workspace(int64_t n) {
+  return static_cast<size_t>(8) << subm_log2cap(n);
+}
+
+int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo, void* workspace,
+                  size_t workspace_bytes, int32_t* gather_map, int64_t* meta, int64_t* status,
+                  void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int rc = check_geometry(geo, false);
+  if (rc != TSC_OK) return rc;
+  TSC_CHECK_ARG(n >= 0 && n <= 0x7fffffffLL, "number of voxels %lld out of range", (long long)n);
+  TSC_CHECK_ARG(meta != nullptr && status != nullptr, "meta/status must not be NULL");
+  const uint64_t cells = cells_of(geo->batch, geo->in_shape);
+  if (cells > kMaxCells) {
+    set_error("grid batch*D*H*W = %llu exceeds the packed-key limit 2^32-2", (unsigned long long)cells);
+    return TSC_ERR_GRID_TOO_LARGE;
+  }
+  const int K = geo->ksize[0] * geo->ksize[1] * geo->ksize[2];
+  TSC_CUDA(cudaMemsetAsync(meta, 0, sizeof(int64_t) * (TSC_META_COUNTS + K), stream));
+  if (n == 0) return TSC_OK;
+  TSC_CHECK_ARG(indices != nullptr && aligned(indices, 16), "indices must be 16-byte aligned");
+  TSC_CHECK_ARG(gather_map != nullptr && aligned(gather_map, 4), "gather_map must not be NULL");
+  const int log2cap = subm_log2cap(n);
+  const size_t need = static_cast<size_t>(8) << log2cap;
+  if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16)) {
+    set_error("subm workspace needs %zu bytes (16-byte aligned), got %zu", need, workspace_bytes);
+    return TSC_ERR_WORKSPACE;
+  }
+  auto* table = static_cast<unsigned long long*>(workspace);
+  TSC_CUDA(cudaMemsetAsync(table, 0xFF, need, stream));
+  const GeoDev g = to_dev(*geo);
+  const int4* idx = reinterpret_cast<const int4*>(indices);
+  const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
+  k_hash_build<<<grid, kThreads, 0, stream>>>(idx, n, g.B, g.D, g.H, g.W, table, log2cap, status);
+  TSC_LAUNCH_CHECK("k_hash_build");
+  k_subm_query<<<dim3(grid, K), kThreads, 0, stream>>>(idx, n, g, table, log2cap, gather_map,
+                                                       reinterpret_cast<unsigned long long*>(meta));
+  TSC_LAUNCH_CHECK("k_subm_query");
+  return TSC_OK;
+}
+
+size_t tsc_strided_kmap_workspace(const tsc_geometry* geo) {
+  if (geo == nullptr) return 0;
+  return strided_ws(*geo).bytes;
+}
+
+int tsc_strided_kmap_count(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
+                           void* workspace, size_t workspace_bytes, int64_t* meta, int64_t* status,
+                           void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int rc = check_geometry(geo, true);
+  if (rc != TSC_OK) return rc;
+  TSC_CHECK_ARG(n_in >= 0 && n_in <= 0x7fffffffLL, "number of voxels %lld out of range", (long long)n_in);
+  TSC_CHECK_ARG(meta != nullptr && status != nullptr, "meta/status must not be NULL");
+  if (cells_of(geo->batch, geo->out_shape) > kMaxCells) {
+    set_error("output grid batch*D*H*W exceeds 2^32-2 cells");
+    return TSC_ERR_GRID_TOO_LARGE;
+  }
+  TSC_CHECK_ARG(n_in == 0 || (indices != nullptr && aligned(indices, 16)),
+                "indices must be 16-byte aligned");
+  const StridedWs w = strided_ws(*geo);
+  if (workspace == nullptr || workspace_bytes < w.bytes || !aligned(workspace, 256)) {
+    set_error("strided workspace needs %zu bytes (256-byte aligned), got %zu", w.bytes, workspace_bytes);
+    return TSC_ERR_WORKSPACE;
+  }
+  const int K = geo->ksize[0] * geo->ksize[1] * geo->ksize[2];
+  char* ws = static_cast<char*>(workspace);
+  auto* bitmap = reinterpret_cast<uint32_t*>(ws);
+  auto* sums = reinterpret_cast<uint32_t*>(ws + w.off_sums);
+  auto* umeta = reinterpret_cast<unsigned long long*>(meta);
+  TSC_CUDA(cudaMemsetAsync(meta, 0, sizeof(int64_t) * (TSC_META_COUNTS + K), stream));
+  TSC_CUDA(cudaMemsetAsync(bitmap, 0, static_cast<size_t>(w.nwords_pad) * 4, stream));
+  const GeoDev g = to_dev(*geo);
+  if (n_in > 0) {
+    const unsigned grid = static_cast<unsigned>(ceil_div(n_in, kThreads));
+    k_strided_mark<<<grid, kThreads, sizeof(unsigned) * (K + 1), stream>>>(
+        reinterpret_cast<const int4*>(indices), n_in, g, bitmap, umeta, status);
+    TSC_LAUNCH_CHECK("k_strided_mark");
+  }
+  k_bitmap_tile_count<<<static_cast<unsigned>(w.nblocks), kThreads, 0, stream>>>(
+      reinterpret_cast<const uint4*>(bitmap), sums);
+  TSC_LAUNCH_CHECK("k_bitmap_tile_count");
+  k_scan_tile_sums<uint32_t><<<1, kScanBlockThreads, 0, stream>>>(sums, w.nblocks, umeta,
+                                                                  TSC_META_N_OUT, status);
+  TSC_LAUNCH_CHECK("k_scan_tile_sums");
+  return TSC_OK;
+}
+
+int tsc_strided_kmap_emit(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
+                          void* workspace, size_t workspace_bytes, int64_t n_out,
+                          int32_t* out_indices, int32_t* gather_map, int32_t* scatter_map,
+                          int32_t* overflow, int64_t overflow_cap, int64_t* meta, int64_t* status,
+                          void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int rc = check_geometry(geo, true);
+  if (rc != TSC_OK) return rc;
+  TSC_CHECK_ARG(n_out >= 0 && n_out <= 0x7fffffffLL, "n_out %lld out of range", (long long)n_out);
+  TSC_CHECK_ARG(meta != nullptr && status != nullptr, "meta/status must not be NULL");
+  const StridedWs w = strided_ws(*geo);
+  if (workspace == nullptr || workspace_bytes < w.bytes || !aligned(workspace, 256)) {
+    set_error("strided workspace needs %zu bytes, got %zu", w.bytes, workspace_bytes);
+    return TSC_ERR_WORKSPACE;
+  }
+  if (n_out == 0 || n_in == 0) return TSC_OK;
+  TSC_CHECK_ARG(indices != nullptr && aligned(indices, 16), "indices must be 16-byte aligned");
+  TSC_CHECK_ARG(out_indices != nullptr && aligned(out_indices, 16), "out_indices must be 16-byte aligned");
+  TSC_CHECK_ARG(gather_map != nullptr && scatter_map != nullptr, "maps must not be NULL");
+  TSC_CHECK_ARG(overflow_cap == 0 || overflow != nullptr, "overflow buffer is NULL");
+  const int K = geo->ksize[0] * geo->ksize[1] * geo->ksize[2];
+  char* ws = static_cast<char*>(workspace);
+  auto* bitmap = reinterpret_cast<uint32_t*>(ws);
+  auto* prefix = reinterpret_cast<uint32_t*>(ws + w.off_prefix);
+  auto* sums = reinterpret_cast<uint32_t*>(ws + w.off_sums);
+  const GeoDev g = to_dev(*geo);
+  k_bitmap_emit<<<static_cast<unsigned>(w.nblocks), kThreads, 0, stream>>>(
+      reinterpret_cast<const uint4*>(bitmap), sums, prefix, g, reinterpret_cast<int4*>(out_indices), n_out);
+  TSC_LAUNCH_CHECK("k_bitmap_emit");
+  TSC_CUDA(cudaMemsetAsync(gather_map, 0xFF, sizeof(int32_t) * static_cast<size_t>(K) * n_out, stream));
+  TSC_CUDA(cudaMemsetAsync(meta + TSC_META_N_OVERFLOW, 0, sizeof(int64_t), stream));
+  const unsigned grid = static_cast<unsigned>(ceil_div(n_in, kThreads));
+  k_strided_pairs<<<grid, kThreads, 0, stream>>>(
+      reinterpret_cast<const int4*>(indices), n_in, g, bitmap, prefix, n_out, gather_map,
+      scatter_map, overflow, overflow_cap, reinterpret_cast<unsigned long long*>(meta), status);
+  TSC_LAUNCH_CHECK("k_strided_pairs");
+  return TSC_OK;
+}
+
+size_t tsc_inverse_kmap_workspace(int64_t n_in) { return rows_scan_bytes(n_in); }
+
+int tsc_inverse_kmap_strided(const int32_t* in_indices, int64_t n_in, const int32_t* scatter_map,
+                             int32_t k_vol, int64_t n_part, void* workspace, size_t workspace_bytes,
+                             int32_t* out_indices, int32_t* inv_gather, int32_t* compact,
+                             int64_t* status, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  TSC_CHECK_ARG(k_vol > 0 && k_vol <= 4096, "kernel volume %d out of range", k_vol);
+  TSC_CHECK_ARG(n_in >= 0 && n_in <= 0x7fffffffLL && n_part >= 0 && n_part <= n_in,
+                "row counts out of range (n_in=%lld, n_part=%lld)", (long long)n_in, (long long)n_part);
+  if (n_in == 0) return TSC_OK;
+  TSC_CHECK_ARG(in_indices != nullptr && aligned(in_indices, 16), "in_indices must be 16-byte aligned");
+  TSC_CHECK_ARG(n_part == 0 || (out_indices != nullptr && aligned(out_indices, 16)),
+                "out_indices must be 16-byte aligned");
+  TSC_CHECK_ARG(scatter_map != nullptr, "scatter_map is NULL");
+  if (n_part == n_in) {
+    // Every forward-input row participates: identity compaction.
+    TSC_CUDA(cudaMemcpyAsync(out_indices, in_indices, sizeof(int32_t) * 4 * static_cast<size_t>(n_in),
+                             cudaMemcpyDeviceToDevice, stream));
+    if (inv_gather != nullptr && inv_gather != scatter_map) {
+      TSC_CUDA(cudaMemcpyAsync(inv_gather, scatter_map, sizeof(int32_t) * static_cast<size_t>(k_vol) * n_in,
+                               cudaMemcpyDeviceToDevice, stream));
+    }
+    if (compact != nullptr) {
+      k_iota<<<static_cast<unsigned>(ceil_div(n_in, kThreads)), kThreads, 0, stream>>>(compact, n_in);
+      TSC_LAUNCH_CHECK("k_iota");
+    }
+    return TSC_OK;
+  }
+  const size_t need = rows_scan_bytes(n_in);
+  if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16)) {
+    set_error("inverse workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    return TSC_ERR_WORKSPACE;
+  }
+  TSC_CHECK_ARG(n_part == 0 || (inv_gather != nullptr && inv_gather != scatter_map),
+                "inv_gather must be a separate buffer");
+  auto* sums = static_cast<uint32_t*>(workspace);
+  const int64_t nblocks = ceil_div(n_in, kTile);
+  k_part_tile_count<<<static_cast<unsigned>(nblocks), kThreads, 0, stream>>>(scatter_map, k_vol, n_in, sums);
+  TSC_LAUNCH_CHECK("k_part_tile_count");
+  k_scan_tile_sums<uint32_t><<<1, kScanBlockThreads, 0, stream>>>(sums, nblocks, nullptr, 0, nullptr);
+  TSC_LAUNCH_CHECK("k_scan_tile_sums");
+  k_inverse_strided_emit<<<static_cast<unsigned>(nblocks), kThreads, 0, stream>>>(
+      reinterpret_cast<const int4*>(in_indices), scatter_map, k_vol, n_in, sums, n_part,
+      reinterpret_cast<int4*>(out_indices), inv_gather, compact);
+  TSC_LAUNCH_CHECK("k_inverse_strided_emit");
+  return TSC_OK;
+}
+
+int tsc_inverse_kmap_subm_count(const int32_t* gather_map, int32_t k_vol, int64_t n, void* workspace,
+                                size_t workspace_bytes, int32_t* compact, int64_t* meta,
+                                int64_t* status, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  TSC_CHECK_ARG(k_vol > 0 && k_vol <= 4096, "kernel volume %d out of range", k_vol);
+  TSC_CHECK_ARG(n >= 0 && n <= 0x7fffffffLL, "row count out of range");
+  TSC_CHECK_ARG(meta != nullptr, "meta is NULL");
+  TSC_CUDA(cudaMemsetAsync(meta + TSC_META_N_PART, 0, sizeof(int64_t), stream));
+  if (n == 0) return TSC_OK;
+  TSC_CHECK_ARG(gather_map != nullptr && compact != nullptr, "maps must not be NULL");
+  const size_t need = rows_scan_bytes(n);
+  if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16)) {
+    set_error("inverse workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    return TSC_ERR_WORKSPACE;
+  }
+  auto* sums = static_cast<uint32_t*>(workspace);
+  const int64_t total = static_cast<int64_t>(k_vol) * n;
+  TSC_CUDA(cudaMemsetAsync(compact, 0, sizeof(int32_t) * static_cast<size_t>(n), stream));
+  k_flag_targets<<<static_cast<unsigned>(ceil_div(total, kThreads)), kThreads, 0, stream>>>(
+      gather_map, total, n, compact);
+  TSC_LAUNCH_CHECK("k_flag_targets");
+  const int64_t nblocks = ceil_div(n, kTile);
+  k_flag_tile_count<<<static_cast<unsigned>(nblocks), kThreads, 0, stream>>>(compact, n, sums);
+  TSC_LAUNCH_CHECK("k_flag_tile_count");
+  k_scan_tile_sums<uint32_t><<<1, kScanBlockThreads, 0, stream>>>(
+      sums, nblocks, reinterpret_cast<unsigned long long*>(meta), TSC_META_N_PART, status);
+  TSC_LAUNCH_CHECK("k_scan_tile_sums");
+  k_flag_compact<<<static_cast<unsigned>(nblocks), kThreads, 0, stream>>>(compact, n, sums);
+  TSC_LAUNCH_CHECK("k_flag_compact");
+  return TSC_OK;
+}
+
+int tsc_inverse_kmap_subm_emit(const int32_t* in_indices, const int32_t* gather_map, int32_t k_vol,
+                               int64_t n, const int32_t* compact, int64_t n_part, int32_t* out_indices,
+                               int32_t* inv_gather, int32_t* overflow, int64_t overflow_cap,
+                               int64_t* meta, int64_t* status, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  TSC_CHECK_ARG(k_vol > 0 && k_vol <= 4096, "kernel volume %d out of range", k_vol);
+  TSC_CHECK_ARG(n >= 0 && n <= 0x7fffffffLL && n_part >= 0 && n_part <= n, "row counts out of range");
+  TSC_CHECK_ARG(meta != nullptr && status != nullptr, "meta/status must not be NULL");
+  TSC_CUDA(cudaMemsetAsync(meta + TSC_META_N_OVERFLOW, 0, sizeof(int64_t), stream));
+  if (n == 0 || n_part == 0) return TSC_OK;
+  TSC_CHECK_ARG(in_indices != nullptr && aligned(in_indices, 16), "in_indices must be 16-byte aligned");
+  TSC_CHECK_ARG(out_indices != nullptr && aligned(out_indices, 16), "out_indices must be 16-byte aligned");
+  TSC_CHECK_ARG(gather_map != nullptr && compact != nullptr && inv_gather != nullptr, "NULL map");
+  TSC_CHECK_ARG(overflow_cap == 0 || overflow != nullptr, "overflow buffer is NULL");
+  k_gather_rows<<<static_cast<unsigned>(ceil_div(n, kThreads)), kThreads, 0, stream>>>(
+      reinterpret_cast<const int4*>(in_indices), compact, n, n_part, reinterpret_cast<int4*>(out_indices));
+  TSC_LAUNCH_CHECK("k_gather_rows");
+  TSC_CUDA(cudaMemsetAsync(inv_gather, 0xFF, sizeof(int32_t) * static_cast<size_t>(k_vol) * n_part, stream));
+  const int64_t total = static_cast<int64_t>(k_vol) * n;
+  k_transpose_map<<<static_cast<unsigned>(ceil_div(total, kThreads)), kThreads, 0, stream>>>(
+      gather_map, k_vol, n, compact, n_part, inv_gather, overflow, overflow_cap,
+      reinterpret_cast<unsigned long long*>(meta), status);
+  TSC_LAUNCH_CHECK("k_transpose_map");
+  return TSC_OK;
+}
+
+size_t tsc_pairs_workspace(int32_t k_vol, int64_t n) {
+  return rows_scan_bytes(static_cast<int64_t>(k_vol) * n);
+}
+
+int tsc_pairs_materialize(const int32_t* map, int32_t k_vol, int64_t n, int32_t mode,
+                          const int32_t* remap, int64_t* pairs_in, int64_t* pairs_out, int64_t capacity,
+                          void* workspace, size_t workspace_bytes, int64_t* status, void* stream_) {
+  (void)status;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  TSC_CHECK_ARG(k_vol > 0 && k_vol <= 4096, "kernel volume %d out of range", k_vol);
+  TSC_CHECK_ARG(mode == 0 || mode == 1, "mode must be 0 or 1");
+  TSC_CHECK_ARG(n >= 0, "row count out of range");
+  const int64_t total = static_cast<int64_t>(k_vol) * n;
+  if (total == 0 || capacity <= 0) return TSC_OK;
+  TSC_CHECK_ARG(map != nullptr && pairs_in != nullptr && pairs_out != nullptr, "NULL buffer");
+  const size_t need = rows_scan_bytes(total);
+  if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16)) {
+    set_error("pairs workspace needs %zu bytes, got %zu", need, workspace_bytes);
+    return TSC_ERR_WORKSPACE;
+  }
+  const int64_t nblocks = ceil_div(total, kTile);
+  TSC_CHECK_ARG(nblocks <= 0x7fffffffLL, "pair map too large");
+  auto* sums = static_cast<unsigned long long*>(workspace);
+  k_map_tile_count<<<static_cast<unsigned>(nblocks), kThreads, 0, stream>>>(map, total, sums);
+  TSC_LAUNCH_CHECK("k_map_tile_count");
+  k_scan_tile_sums<unsigned long long><<<1, kScanBlockThreads, 0, stream>>>(sums, nblocks, nullptr, 0, nullptr);
+  TSC_LAUNCH_CHECK("k_scan_tile_sums");
+  k_map_emit_pairs<<<static_cast<unsigned>(nblocks), kThreads, 0, stream>>>(
+      map, total, n, mode, remap, sums, pairs_in, pairs_out, capacity);
+  TSC_LAUNCH_CHECK("k_map_emit_pairs");
+  return TSC_OK;
+}
+
+int tsc_gather_from_pairs(const int64_t* pairs_in, const int64_t* pairs_out, const int64_t* offsets_host,
+                          int32_t k_vol, int64_t n_out, int32_t* gather_map, int32_t* overflow,
+                          int64_t overflow_cap, int64_t* meta, int64_t* status, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  TSC_CHECK_ARG(k_vol > 0 && k_vol <= 4096, "kernel volume %d out of range", k_vol);
+  TSC_CHECK_ARG(n_out >= 0 && n_out <= 0x7fffffffLL, "n_out out of range");
+  TSC_CHECK_ARG(offsets_host != nullptr && meta != nullptr && status != nullptr, "NULL argument");
+  TSC_CUDA(cudaMemsetAsync(meta + TSC_META_N_OVERFLOW, 0, sizeof(int64_t), stream));
+  if (n_out == 0) return TSC_OK;
+  TSC_CHECK_ARG(gather_map != nullptr, "gather_map is NULL");
+  TSC_CHECK_ARG(overflow_cap == 0 || overflow != nullptr, "overflow buffer is NULL");
+  TSC_CUDA(cudaMemsetAsync(gather_map, 0xFF, sizeof(int32_t) * static_cast<size_t>(k_vol) * n_out, stream));
+  for (int k = 0; k < k_vol; ++k) {
+    const int64_t b = offsets_host[k], e = offsets_host[k + 1];
+    TSC_CHECK_ARG(b >= 0 && e >= b, "pair offsets are not monotone at k=%d", k);
+    if (e == b) continue;
+    k_pairs_to_gather<<<static_cast<unsigned>(ceil_div(e - b, kThreads)), kThreads, 0, stream>>>(
+        pairs_in + b, pairs_out + b, e - b, k, n_out, gather_map, overflow, overflow_cap,
+        reinterpret_cast<unsigned long long*>(meta), status);
+    TSC_LAUNCH_CHECK("k_pairs_to_gather");
+  }
+  return TSC_OK;
+}
+
+}  // extern "C"

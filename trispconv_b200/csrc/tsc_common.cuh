@@ -1,0 +1,161 @@
+// Shared device/host helpers for the trispconv_b200 CUDA library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "trispconv_b200.h"
+
+namespace tsc {
+
+// ---- host-side error reporting ------------------------------------------------
+void set_error(const char* fmt, ...);
+void count_launch();
+// Checks cudaGetLastError() after a launch; records `what` on failure.
+int check_launch(const char* what);
+
+#define TSC_CHECK_ARG(cond, ...)                                             \
+  do {                                                                       \
+    if (!(cond)) {                                                           \
+      ::tsc::set_error(__VA_ARGS__);                                         \
+      return TSC_ERR_INVALID_ARG;                                            \
+    }                                                                        \
+  } while (0)
+
+#define TSC_CUDA(call)                                                       \
+  do {                                                                       \
+    cudaError_t e_ = (call);                                                 \
+    if (e_ != cudaSuccess) {                                                 \
+      ::tsc::set_error("%s failed: %s", #call, cudaGetErrorString(e_));      \
+      return TSC_ERR_CUDA;                                                   \
+    }                                                                        \
+  } while (0)
+
+#define TSC_LAUNCH_CHECK(what)                                               \
+  do {                                                                       \
+    ::tsc::count_launch();                                                   \
+    int rc_ = ::tsc::check_launch(what);                                     \
+    if (rc_ != TSC_OK) return rc_;                                           \
+  } while (0)
+
+inline bool aligned(const void* p, size_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Cached multiprocessor count of the current device.
+int sm_count();
+
+// ---- device helpers -------------------------------------------------------------
+constexpr unsigned long long kEmptySlot = ~0ull;
+constexpr unsigned kFullMask = 0xffffffffu;
+
+__device__ __forceinline__ void raise_status(int64_t* status, long long bits) {
+  atomicOr(reinterpret_cast<unsigned long long*>(status), static_cast<unsigned long long>(bits));
+}
+
+// Fibonacci hashing of a 32-bit linear cell key into a power-of-two table.
+__device__ __forceinline__ uint32_t hash_slot(uint32_t key, int log2cap) {
+  return static_cast<uint32_t>((static_cast<unsigned long long>(key) * 0x9E3779B97F4A7C15ull) >>
+                               (64 - log2cap));
+}
+
+// Kernel offset decomposition, k = (kz*kH + ky)*kW + kx.
+struct KOffset {
+  int kz, ky, kx;
+};
+__device__ __forceinline__ KOffset split_k(int k, int kH, int kW) {
+  KOffset r;
+  r.kx = k % kW;
+  int t = k / kW;
+  r.ky = t % kH;
+  r.kz = t / kH;
+  return r;
+}
+
+// Element conversions.
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// Block-wide exclusive scan of one uint32 per thread (blockDim.x multiple of 32,
+// at most 1024).  `warp_sums` must hold 32 entries.  Returns the exclusive prefix
+// and writes the block total to *total.
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_sums,
+                                                         uint32_t* total) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    uint32_t y = __shfl_up_sync(kFullMask, x, d);
+    if (lane >= d) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < nwarps ? warp_sums[lane] : 0u;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      uint32_t y = __shfl_up_sync(kFullMask, w, d);
+      if (lane >= d) w += y;
+    }
+    if (lane < nwarps) warp_sums[lane] = w;  // inclusive warp prefix
+  }
+  __syncthreads();
+  uint32_t warp_off = warp > 0 ? warp_sums[warp - 1] : 0u;
+  uint32_t tot = warp_sums[nwarps - 1];
+  __syncthreads();  // warp_sums may be reused by the caller right after
+  *total = tot;
+  return warp_off + x - v;
+}
+
+// 64-bit variant for offsets that may exceed 2^32 (pair lists).
+__device__ __forceinline__ unsigned long long block_exclusive_scan64(unsigned long long v,
+                                                                     unsigned long long* warp_sums,
+                                                                     unsigned long long* total) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  unsigned long long x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    unsigned long long y = __shfl_up_sync(kFullMask, x, d);
+    if (lane >= d) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    unsigned long long w = lane < nwarps ? warp_sums[lane] : 0ull;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      unsigned long long y = __shfl_up_sync(kFullMask, w, d);
+      if (lane >= d) w += y;
+    }
+    if (lane < nwarps) warp_sums[lane] = w;
+  }
+  __syncthreads();
+  unsigned long long warp_off = warp > 0 ? warp_sums[warp - 1] : 0ull;
+  unsigned long long tot = warp_sums[nwarps - 1];
+  __syncthreads();
+  *total = tot;
+  return warp_off + x - v;
+}
+
+}  // namespace tsc

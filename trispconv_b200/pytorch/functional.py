@@ -1,0 +1,96 @@
+"""Sparse convolution forward (functional.py:14-51 of the reference).
+
+One launch of the output-stationary implicit-GEMM kernel in
+libtrispconv_b200.so per layer, for every dtype; there is no PyTorch, CPU or
+Triton path.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from trispconv_b200 import _lib as L
+from trispconv_b200.pytorch.indices import IndiceData, KernelMap, kmap_from_pairs
+
+SUPPORTED_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
+
+
+def kernel_map_for(indice_data: IndiceData, n_out: int, device: torch.device) -> KernelMap:
+    """Device kernel map of `indice_data` sized for n_out outputs (built from
+    the explicit pair lists when the IndiceData was assembled by hand)."""
+    km = indice_data._kmap
+    if km is not None and km.n_out == n_out and km.gather is not None:
+        return km
+    km = kmap_from_pairs(indice_data.pairs_in, indice_data.pairs_out, n_out, device)
+    if indice_data._kmap is None:
+        indice_data._kmap = km
+    return km
+
+
+def _as_dtype(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    t = t.detach()
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    return L.aligned(t, 16)
+
+
+def conv_launch(features: torch.Tensor, weight: torch.Tensor, weight_layout: int,
+                bias: Optional[torch.Tensor], km: Optional[KernelMap], n_out: int, c_out: int,
+                relu: bool = False) -> torch.Tensor:
+    """One tsc_conv_forward launch.  `weight` is (K, Cin, Cout) for W_KCC or
+    (Cout, kD, kH, kW, Cin) for W_KRSC; km None means the identity map."""
+    dev = features.device
+    dtype = features.dtype
+    n_in, c_in = features.shape
+    out = torch.empty((n_out, c_out), dtype=dtype, device=dev)
+    if n_out == 0:
+        return out
+    feats = L.aligned(features, 16)
+    w = _as_dtype(weight, dtype)
+    b = None if bias is None else _as_dtype(bias.reshape(-1), dtype)
+    if km is None:
+        gather = overflow = meta = None
+        cap, k_vol = 0, 1
+    else:
+        gather, overflow, meta, cap, k_vol = km.gather, km.overflow, km.meta, km.overflow_cap, km.k_vol
+    lib = L.load()
+    rc = lib.tsc_conv_forward(feats.data_ptr() if n_in else None, L.DTYPE_CODE[dtype], n_in, c_in,
+                              w.data_ptr(), weight_layout, L.ptr(b), L.ptr(gather), k_vol, n_out, c_out,
+                              L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(),
+                              L.CONV_RELU if relu else 0, L.status_word(dev).data_ptr(), L.stream_ptr(dev))
+    L.check(rc, "tsc_conv_forward")
+    if L.EAGER_CHECKS:
+        L.check_device_status(dev)
+    return out
+
+
+def check_features(features: torch.Tensor) -> None:
+    L.require_cuda(features, "features")
+    if features.dtype not in SUPPORTED_DTYPES:
+        raise NotImplementedError(
+            f"trispconv_b200 computes in float32/float16/bfloat16, got {features.dtype}")
+    if features.ndim != 2:
+        raise ValueError(f"features must be (N, C), got {tuple(features.shape)}")
+
+
+def sparse_conv_forward(features: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
+                        indice_data: IndiceData, N_out: int, *, relu: bool = False) -> torch.Tensor:
+    """out[N_out, C_out] = sum_k features[in_k] @ weight[k] scattered to out_k,
+    + bias, in features.dtype with fp32 accumulation.
+
+    weight must be in the internal (Kvol, C_in, C_out) layout.  ``relu``
+    fuses a following ReLU into the store (used by SparseSequential)."""
+    check_features(features)
+    if weight.ndim != 3:
+        raise ValueError(f"weight must be (Kvol, C_in, C_out), got {tuple(weight.shape)}")
+    if weight.shape[1] != features.shape[1]:
+        raise RuntimeError(
+            f"features have {features.shape[1]} channels but weight expects {weight.shape[1]}")
+    N_out = int(N_out)
+    km = kernel_map_for(indice_data, N_out, features.device) if N_out > 0 else None
+    if km is not None and weight.shape[0] < km.k_vol:
+        raise IndexError(f"weight has {weight.shape[0]} kernel slots, the indice pairs use {km.k_vol}")
+    if km is not None and weight.shape[0] != km.k_vol:
+        weight = weight[: km.k_vol]
+    return conv_launch(features, weight, L.W_KCC, bias, km, N_out, weight.shape[2], relu=relu)

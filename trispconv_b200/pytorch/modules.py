@@ -1,0 +1,236 @@
+"""Sparse convolution modules (modules.py:20-329 of the reference).
+
+Constructors, parameters (KRSC ``weight``, ``bias``), indice_key caching and
+error behaviour follow the reference; the forward passes call the CUDA
+kernel-map builders and the implicit-GEMM kernel.  Differences a user can
+see: tensors must be on a CUDA device, and outputs carry no autograd graph
+(the reference is an inference library as well).
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional, Tuple, Union
+
+import torch
+import torch.nn as nn
+
+from trispconv_b200 import _lib as L
+from trispconv_b200.pytorch.functional import check_features, conv_launch, kernel_map_for
+from trispconv_b200.pytorch.indices import (
+    IndiceData,
+    _to3,
+    generate_strided_indice_pairs,
+    generate_subm_indice_pairs,
+    inverse_indice_data,
+)
+from trispconv_b200.pytorch.tensor import SparseConvTensor
+from trispconv_b200.pytorch.weight import normalize_spconv_weight
+
+FUSE_RELU = os.environ.get("TRISPCONV_B200_FUSE", "1") != "0"
+
+
+class SparseModule(nn.Module):
+    """Marker base class for modules that consume and produce SparseConvTensor."""
+
+
+class SparseConvolution(SparseModule):
+    def __init__(self, ndim: int, in_channels: int, out_channels: int, kernel_size, stride=1, padding=0,
+                 dilation=1, groups: int = 1, bias: bool = True, subm: bool = False, output_padding=0,
+                 transposed: bool = False, inverse: bool = False, indice_key: Optional[str] = None,
+                 algo=None):
+        super().__init__()
+        if ndim != 3:
+            raise NotImplementedError(f"Only ndim=3 is supported, got ndim={ndim}")
+        if groups != 1:
+            raise NotImplementedError("Grouped convolution is not supported")
+        if transposed and not inverse:
+            raise NotImplementedError("Transposed convolution is not supported; use SparseInverseConv3d")
+        self.ndim = ndim
+        self.in_channels = in_channels
+        self.out_channels = out_channels
+        self.kernel_size = _to3(kernel_size)
+        self.stride = _to3(stride)
+        self.padding = _to3(padding)
+        self.dilation = _to3(dilation)
+        self.subm = subm
+        self.inverse = inverse
+        self.indice_key = indice_key
+        kD, kH, kW = self.kernel_size
+        k_vol = kD * kH * kW
+        # spconv KRSC parameter (C_out, kD, kH, kW, C_in): checkpoint compatible.
+        self.weight = nn.Parameter(torch.empty(out_channels, kD, kH, kW, in_channels))
+        self.bias = nn.Parameter(torch.zeros(out_channels)) if bias else None
+        nn.init.kaiming_uniform_(self.weight.data.reshape(out_channels, k_vol * in_channels))
+
+    # -- weights --------------------------------------------------------------
+    def _get_weight(self) -> torch.Tensor:
+        """Internal (Kvol, C_in, C_out) weight, as the reference computes it."""
+        return normalize_spconv_weight(self.weight, self.kernel_size, self.in_channels, self.out_channels)
+
+    def _kernel_weight(self, k_used: int) -> Tuple[torch.Tensor, int]:
+        """(tensor, layout) read in place by the conv kernel for the first
+        `k_used` kernel slots."""
+        kD, kH, kW = self.kernel_size
+        k_vol = kD * kH * kW
+        if k_used > k_vol:
+            raise IndexError(f"module has {k_vol} kernel slots, the indice pairs use {k_used}")
+        w = self.weight
+        cin, cout = self.in_channels, self.out_channels
+        shape = tuple(w.shape)
+        if k_used == k_vol:
+            if shape == (cout, kD, kH, kW, cin):
+                if k_vol == 1:  # spconv 1x1x1: flat KRSC storage read as (C_in, C_out)
+                    return w.reshape(1, cin, cout), L.W_KCC
+                return w, L.W_KRSC
+            if k_vol == 1 and shape == (cout, cin):
+                return w.reshape(1, cin, cout), L.W_KCC
+        return normalize_spconv_weight(w, self.kernel_size, cin, cout)[:k_used], L.W_KCC
+
+    def _conv(self, features: torch.Tensor, data: Optional[IndiceData], n_out: int, relu: bool) -> torch.Tensor:
+        if features.shape[1] != self.in_channels:
+            raise RuntimeError(f"features have {features.shape[1]} channels, "
+                               f"{type(self).__name__} expects {self.in_channels}")
+        km = None
+        if data is not None and n_out > 0:
+            km = kernel_map_for(data, n_out, features.device)
+        k_used = km.k_vol if km is not None else 1
+        w, layout = self._kernel_weight(k_used)
+        return conv_launch(features, w, layout, self.bias, km, n_out, self.out_channels, relu=relu)
+
+    # -- forward ------------------------------------------------------------------
+    def forward(self, x: SparseConvTensor) -> SparseConvTensor:
+        return self._forward_impl(x, relu=False)
+
+    def _forward_impl(self, x: SparseConvTensor, relu: bool) -> SparseConvTensor:
+        check_features(x.features)
+        L.require_cuda(x.indices, "indices")
+        with torch.no_grad():
+            if self.inverse:
+                return self._forward_inverse(x, relu)
+            if self.subm:
+                return self._forward_subm(x, relu)
+            return self._forward_strided(x, relu)
+
+    def _get_or_compute_subm_indice(self, x: SparseConvTensor) -> IndiceData:
+        if self.indice_key is not None and self.indice_key in x.indice_dict:
+            return x.indice_dict[self.indice_key]
+        data = generate_subm_indice_pairs(x.indices, tuple(x.spatial_shape), x.batch_size,
+                                          self.kernel_size, self.dilation)
+        if self.indice_key is not None:
+            x.indice_dict[self.indice_key] = data
+        return data
+
+    def _get_or_compute_strided_indice(self, x: SparseConvTensor) -> IndiceData:
+        if self.indice_key is not None and self.indice_key in x.indice_dict:
+            return x.indice_dict[self.indice_key]
+        data = generate_strided_indice_pairs(x.indices, tuple(x.spatial_shape), x.batch_size,
+                                             self.kernel_size, self.stride, self.padding, self.dilation)
+        if self.indice_key is not None:
+            x.indice_dict[self.indice_key] = data
+        return data
+
+    def _forward_subm(self, x: SparseConvTensor, relu: bool = False) -> SparseConvTensor:
+        data = self._get_or_compute_subm_indice(x)
+        n_out = len(data.out_indices)
+        out = self._conv(x.features, data, n_out, relu)
+        return SparseConvTensor(out, data.out_indices, x.spatial_shape, x.batch_size,
+                                indice_dict=x.indice_dict)
+
+    def _forward_strided(self, x: SparseConvTensor, relu: bool = False) -> SparseConvTensor:
+        data = self._get_or_compute_strided_indice(x)
+        n_out = len(data.out_indices)
+        out = self._conv(x.features, data, n_out, relu)
+        return SparseConvTensor(out, data.out_indices, list(data.output_spatial_shape), x.batch_size,
+                                indice_dict=x.indice_dict)
+
+    def _forward_inverse(self, x: SparseConvTensor, relu: bool = False) -> SparseConvTensor:
+        if self.indice_key is None:
+            raise ValueError("SparseInverseConv3d requires indice_key")
+        if self.indice_key not in x.indice_dict:
+            raise KeyError(
+                f"indice_key '{self.indice_key}' not found in indice_dict. "
+                "The paired SparseConv3d must run before SparseInverseConv3d.")
+        fwd: IndiceData = x.indice_dict[self.indice_key]
+        kD, kH, kW = fwd.kernel_size
+        if kD == 1 and kH == 1 and kW == 1:
+            # spconv 1x1x1 fast path: output stays in the inverse input's space
+            # (modules.py:160-173).
+            out = self._conv(x.features, None, x.features.shape[0], relu)
+            return SparseConvTensor(out, x.indices, x.spatial_shape, x.batch_size,
+                                    indice_dict=x.indice_dict)
+        inv = getattr(fwd, "_inverse_cache", None)
+        if inv is None:
+            inv = inverse_indice_data(fwd)
+            fwd._inverse_cache = inv
+        data, n_out = inv
+        out = self._conv(x.features, data, n_out, relu)
+        return SparseConvTensor(out, data.out_indices, list(fwd.input_spatial_shape), x.batch_size,
+                                indice_dict=x.indice_dict)
+
+
+class SubMConv3d(SparseConvolution):
+    def __init__(self, in_channels: int, out_channels: int, kernel_size, stride=1, padding=0, dilation=1,
+                 bias: bool = True, indice_key: Optional[str] = None, algo=None):
+        super().__init__(ndim=3, in_channels=in_channels, out_channels=out_channels,
+                         kernel_size=kernel_size, stride=1, padding=0, dilation=dilation, bias=bias,
+                         subm=True, indice_key=indice_key, algo=algo)
+
+
+class SparseConv3d(SparseConvolution):
+    def __init__(self, in_channels: int, out_channels: int, kernel_size, stride=1, padding=0, dilation=1,
+                 bias: bool = True, indice_key: Optional[str] = None, algo=None):
+        super().__init__(ndim=3, in_channels=in_channels, out_channels=out_channels,
+                         kernel_size=kernel_size, stride=stride, padding=padding, dilation=dilation,
+                         bias=bias, subm=False, indice_key=indice_key, algo=algo)
+
+
+class SparseInverseConv3d(SparseConvolution):
+    def __init__(self, in_channels: int, out_channels: int, kernel_size, bias: bool = True,
+                 indice_key: Optional[str] = None, algo=None):
+        super().__init__(ndim=3, in_channels=in_channels, out_channels=out_channels,
+                         kernel_size=kernel_size, stride=1, padding=0, dilation=1, bias=bias,
+                         subm=False, inverse=True, indice_key=indice_key, algo=algo)
+
+
+def _fusable(conv: nn.Module, act: nn.Module) -> bool:
+    """conv followed by a plain ReLU, no hooks, no forward override."""
+    return (FUSE_RELU and isinstance(conv, SparseConvolution) and type(act) is nn.ReLU
+            and type(conv).forward is SparseConvolution.forward
+            and not conv._forward_hooks and not conv._forward_pre_hooks
+            and not act._forward_hooks and not act._forward_pre_hooks)
+
+
+class SparseSequential(SparseModule):
+    """Sequential container; dense modules (BN, ReLU, ...) get x.features
+    (modules.py:306-329).  A SparseConvolution directly followed by nn.ReLU
+    runs as one kernel with the ReLU applied in its store."""
+
+    def __init__(self, *args, **kwargs):
+        super().__init__()
+        if len(args) == 1 and isinstance(args[0], dict):
+            for key, module in args[0].items():
+                self.add_module(key, module)
+        else:
+            for idx, module in enumerate(args):
+                self.add_module(str(idx), module)
+        for key, module in kwargs.items():
+            self.add_module(key, module)
+
+    def forward(self, x: Union[SparseConvTensor, torch.Tensor]) -> Union[SparseConvTensor, torch.Tensor]:
+        mods = list(self.children())
+        i = 0
+        while i < len(mods):
+            module = mods[i]
+            if isinstance(x, SparseConvTensor):
+                if i + 1 < len(mods) and _fusable(module, mods[i + 1]):
+                    x = module._forward_impl(x, relu=True)
+                    i += 2
+                    continue
+                if isinstance(module, SparseModule):
+                    x = module(x)
+                else:
+                    x = x.replace_feature(module(x.features))
+            else:
+                x = module(x)
+            i += 1
+        return x
