@@ -55,6 +55,7 @@ extern "C" {
 #define TSC_STATUS_KEY_RANGE      0x1  /* a coordinate lies outside [0,batch) x spatial_shape */
 #define TSC_STATUS_HASH_FULL      0x2  /* open-addressing table ran out of probes */
 #define TSC_STATUS_OVERFLOW_FULL  0x4  /* duplicate-pair overflow list ran out of room */
+#define TSC_STATUS_WAIT_TIMEOUT   0x8  /* a kernel gave up waiting on one of its own barriers */
 
 /* Feature / weight element types. */
 #define TSC_F32  0
@@ -63,7 +64,9 @@ extern "C" {
 #define TSC_F64  3
 
 /* Conv flags. */
-#define TSC_CONV_RELU 0x1
+#define TSC_CONV_RELU       0x1
+#define TSC_CONV_FORCE_SIMT 0x100  /* testing: use the CUDA-core kernel even when a tensor-core one applies */
+#define TSC_CONV_USE_TC     0x200  /* use the tcgen05 (TMEM) kernel where it applies */
 
 /* Weight layouts accepted by tsc_conv_forward. */
 #define TSC_W_KCC  0  /* (K, C_in, C_out): the reference's internal layout (weight.py:36) */
@@ -201,10 +204,15 @@ TSC_API int tsc_gather_from_pairs(const int64_t* pairs_in, const int64_t* pairs_
  * overflow (capacity overflow_cap triples) and meta carry the
  * duplicate-coordinate pairs of the kernel-map builders; the kernel reads
  * their count from meta[TSC_META_N_OVERFLOW] on the device.  Pass NULL when
- * the map cannot have any (submanifold maps). */
+ * the map cannot have any (submanifold maps).  row_order (NULL = identity)
+ * is a permutation of [0, n_out) giving the order in which output rows are
+ * grouped into tiles; results do not depend on it.  16-bit dtypes with KRSC
+ * weights, C_in % 8 == 0 (or C_in % 4 == 0 and C_in <= 16), C_out % 8 == 0
+ * and K <= 64 run on the tensor cores; everything else on the CUDA cores. */
 TSC_API int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t c_in,
                      const void* weight, int32_t weight_layout, const void* bias,
-                     const int32_t* gather_map, int32_t k_vol, int64_t n_out, int32_t c_out,
+                     const int32_t* gather_map, const int32_t* row_order,
+                     int32_t k_vol, int64_t n_out, int32_t c_out,
                      const int32_t* overflow, int64_t overflow_cap, const int64_t* meta,
                      void* out, int32_t flags, int64_t* status, void* stream);
 

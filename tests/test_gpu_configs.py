@@ -87,6 +87,15 @@ def test_config5_kernel_map(cuda):
     _check_digests("config5", wl, seen)
 
 
+_C5_PAIRS = {}
+
+
+def _config5_pairs(wl):
+    if "p" not in _C5_PAIRS:
+        _C5_PAIRS["p"] = oracle.subm_pairs(wl.indices, wl.spatial_shape, wl.batch_size, 3)
+    return _C5_PAIRS["p"]
+
+
 @pytest.mark.parametrize("channels", [64, 128, 256])
 def test_config5_features_rows(cuda, channels):
     """Full batch of 16 x 500k voxels on the GPU; the oracle recomputes a
@@ -96,7 +105,7 @@ def test_config5_features_rows(cuda, channels):
     rng = np.random.default_rng(channels)
     rows = np.sort(rng.choice(wl.n_voxels, 20000, replace=False))
     spec = wl.layers[0]
-    pairs = oracle.subm_pairs(wl.indices, wl.spatial_shape, wl.batch_size, 3)
+    pairs = _config5_pairs(wl)
     w = oracle.normalize_weight(spec["weight"].astype(np.float32), (3, 3, 3), channels, channels)
     want = np.zeros((len(rows), channels), np.float32)
     pos = np.full(wl.n_voxels, -1, np.int64)

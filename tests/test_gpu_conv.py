@@ -274,3 +274,36 @@ def test_dense_matches_host_scatter(cuda):
     bad[0, 2] = 99
     with pytest.raises(AssertionError):
         spconv.SparseConvTensor(f, bad, [5, 6, 7], 2).dense()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
+@pytest.mark.parametrize("cin,cout,ks", [(4, 16, 3), (12, 8, 3), (16, 32, 3), (32, 32, 2), (64, 64, 3),
+                                         (96, 136, 3), (128, 256, 3), (64, 24, 1), (20, 16, 3)])
+def test_tensor_core_matches_cuda_core_kernel(cuda, dtype, cin, cout, ks):
+    """Same inputs through the mma.sync kernel and the fp32-FFMA kernel
+    (TRISPCONV_B200_FORCE_SIMT path): both accumulate in fp32, so they agree
+    to within fp32 summation-order differences before the final rounding."""
+    from trispconv_b200.pytorch import functional as Fn
+
+    rng = np.random.default_rng(cin + 7 * cout + ks)
+    shape = (20, 20, 20)
+    n = 2500
+    cells = rng.choice(np.prod(shape), n, replace=False)
+    z, y, x = np.unravel_index(cells, shape)
+    idx = torch.from_numpy(np.stack([np.zeros(n), z, y, x], 1).astype(np.int32)).to(cuda)
+    f = torch.from_numpy(rng.standard_normal((n, cin)).astype(np.float32)).to(cuda, dtype)
+    for kind in ("subm", "spconv"):
+        m = (spconv.SubMConv3d(cin, cout, ks) if kind == "subm" else
+             spconv.SparseConv3d(cin, cout, ks, stride=2, padding=1)).to(cuda, dtype)
+        x_ = spconv.SparseConvTensor(f, idx, shape, 1)
+        a = m(x_)
+        Fn.set_force_simt(True)
+        try:
+            b = m(spconv.SparseConvTensor(f, idx, shape, 1))
+        finally:
+            Fn.set_force_simt(False)
+        assert torch.equal(a.indices, b.indices)
+        scale = b.features.float().abs().max().item()
+        err = (a.features.float() - b.features.float()).abs().max().item()
+        ulp = 2 ** -7 if dtype == torch.bfloat16 else 2 ** -10
+        assert err <= 2 * ulp * max(scale, 1e-3), (kind, err, scale)

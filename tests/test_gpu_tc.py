@@ -1,0 +1,118 @@
+"""The tcgen05 / tensor-memory convolution kernel against the fp32 CUDA-core
+kernel on identical inputs (both accumulate in fp32; they may differ only by
+summation order before the single 16-bit rounding) and against the oracle."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import trispconv_b200.pytorch as spconv
+from gpu_util import assert_close_rel, np_
+from trispconv_b200.pytorch import functional as Fn
+
+pytestmark = pytest.mark.gpu
+
+
+def _cloud(rng, shape, n):
+    cells = rng.choice(int(np.prod(shape)), n, replace=False)
+    z, y, x = np.unravel_index(cells, shape)
+    return np.stack([np.zeros(n), z, y, x], 1).astype(np.int32)
+
+
+def _run_both(m, x_fn):
+    Fn.set_tensor_memory_path(True)
+    try:
+        a = m(x_fn())
+    finally:
+        Fn.set_tensor_memory_path(False)
+    Fn.set_force_simt(True)
+    try:
+        b = m(x_fn())
+    finally:
+        Fn.set_force_simt(False)
+    torch.cuda.synchronize()
+    return a, b
+
+
+def _assert_same(a, b, dtype, what):
+    assert torch.equal(a.indices, b.indices), what
+    assert torch.isfinite(a.features).all(), what
+    scale = b.features.float().abs().max().item()
+    err = (a.features.float() - b.features.float()).abs().max().item()
+    ulp = 2 ** -7 if dtype == torch.bfloat16 else 2 ** -10
+    assert err <= 2 * ulp * max(scale, 1e-3), (what, err, scale)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
+@pytest.mark.parametrize("cin,cout", [(64, 64), (16, 32), (32, 64), (64, 128), (128, 128), (128, 256),
+                                      (256, 256), (96, 40), (8, 24), (192, 512)])
+def test_tc_matches_cuda_core(cuda, dtype, cin, cout):
+    rng = np.random.default_rng(cin * 31 + cout)
+    shape = (18, 20, 22)
+    idx = torch.from_numpy(_cloud(rng, shape, 3001)).to(cuda)  # not a multiple of 128 rows
+    f = torch.from_numpy(rng.standard_normal((3001, cin)).astype(np.float32)).to(cuda, dtype)
+    for kind in ("subm", "spconv"):
+        m = (spconv.SubMConv3d(cin, cout, 3) if kind == "subm" else
+             spconv.SparseConv3d(cin, cout, 3, stride=2, padding=1)).to(cuda, dtype)
+        with torch.no_grad():
+            m.weight.mul_(0.5)
+            m.bias.normal_(0, 0.1)
+        a, b = _run_both(m, lambda: spconv.SparseConvTensor(f, idx, shape, 1))
+        _assert_same(a, b, dtype, f"{kind} {cin}->{cout}")
+
+
+def test_tc_vs_oracle_and_relu(cuda):
+    rng = np.random.default_rng(2)
+    shape = (16, 16, 16)
+    idx = _cloud(rng, shape, 2000)
+    f = rng.standard_normal((2000, 64)).astype(np.float32)
+    w = (rng.standard_normal((64, 3, 3, 3, 64)) / np.sqrt(27 * 64)).astype(np.float32)
+    b = (rng.standard_normal(64) * 0.1).astype(np.float32)
+    spec = dict(type="subm", cin=64, cout=64, ksize=3, stride=1, padding=0, dilation=1, key=None, weight=w,
+                bias=b, relu=True)
+    ref = oracle.network.conv_layer(oracle.network.OracleTensor(f.astype(np.float16).astype(np.float32), idx,
+                                                                shape, 1), spec)
+    m = spconv.SubMConv3d(64, 64, 3).to(cuda)
+    with torch.no_grad():
+        m.weight.copy_(torch.from_numpy(w))
+        m.bias.copy_(torch.from_numpy(b))
+    m = m.half()
+    seq = spconv.SparseSequential(m, torch.nn.ReLU())
+    Fn.set_tensor_memory_path(True)
+    try:
+        y = seq(spconv.SparseConvTensor(torch.from_numpy(f).to(cuda).half(), torch.from_numpy(idx).to(cuda),
+                                        shape, 1))
+    finally:
+        Fn.set_tensor_memory_path(False)
+    assert_close_rel(np_(y.features.float()), ref.features, 1e-2, "tcgen05 SubM + fused ReLU")
+    from trispconv_b200 import _lib
+
+    _lib.check_device_status(cuda)
+
+
+def test_tc_duplicates_use_overflow(cuda):
+    rng = np.random.default_rng(4)
+    base = rng.integers(0, 10, (300, 3))
+    xyz = np.concatenate([base, base[:120]])
+    idx = np.concatenate([np.zeros((len(xyz), 1), int), xyz], 1).astype(np.int32)
+    f = torch.from_numpy(rng.standard_normal((len(idx), 32)).astype(np.float32)).to(cuda).half()
+    it = torch.from_numpy(idx).to(cuda)
+    m = spconv.SparseConv3d(32, 64, 3, stride=2, padding=1).to(cuda).half()
+    a, b = _run_both(m, lambda: spconv.SparseConvTensor(f, it, [10, 10, 10], 1))
+    _assert_same(a, b, torch.float16, "duplicates")
+
+
+def test_tc_one_by_one_and_empty_tiles(cuda):
+    rng = np.random.default_rng(5)
+    shape = (8, 8, 8)
+    idx = torch.from_numpy(_cloud(rng, shape, 200)).to(cuda)
+    f = torch.from_numpy(rng.standard_normal((200, 32)).astype(np.float32)).to(cuda).half()
+    m = spconv.SubMConv3d(32, 48, 1).to(cuda).half()  # 1x1x1 quirk, KCC weight -> transposed
+    a, b = _run_both(m, lambda: spconv.SparseConvTensor(f, idx, shape, 1))
+    _assert_same(a, b, torch.float16, "1x1x1")
+    # isolated voxels: most offsets have no pair in any tile
+    far = torch.tensor([[0, 0, 0, 0], [0, 7, 7, 7], [0, 0, 7, 0]], dtype=torch.int32, device=cuda)
+    m3 = spconv.SubMConv3d(32, 32, 3).to(cuda).half()
+    fa = f[:3].contiguous()
+    a, b = _run_both(m3, lambda: spconv.SparseConvTensor(fa, far, shape, 1))
+    _assert_same(a, b, torch.float16, "isolated")

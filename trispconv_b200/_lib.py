@@ -27,6 +27,7 @@ TSC_ERR_GRID_TOO_LARGE = 5
 STATUS_KEY_RANGE = 0x1
 STATUS_HASH_FULL = 0x2
 STATUS_OVERFLOW_FULL = 0x4
+STATUS_WAIT_TIMEOUT = 0x8
 
 META_N_OUT = 0
 META_N_PART = 1
@@ -35,6 +36,8 @@ META_STATUS = 4
 META_COUNTS = 8
 
 CONV_RELU = 0x1
+CONV_FORCE_SIMT = 0x100
+CONV_USE_TC = 0x200
 
 W_KCC = 0   # (K, C_in, C_out)
 W_KRSC = 1  # (C_out, kD, kH, kW, C_in)
@@ -87,8 +90,8 @@ _SIGNATURES = {
     "tsc_pairs_materialize": (ctypes.c_int, [_P, c_int32, c_int64, c_int32, _P, _P, _P, c_int64, _P, c_size_t,
                                              _P, _P]),
     "tsc_gather_from_pairs": (ctypes.c_int, [_P, _P, _P, c_int32, c_int64, _P, _P, c_int64, _P, _P, _P]),
-    "tsc_conv_forward": (ctypes.c_int, [_P, c_int32, c_int64, c_int32, _P, c_int32, _P, _P, c_int32, c_int64,
-                                        c_int32, _P, c_int64, _P, _P, c_int32, _P, _P]),
+    "tsc_conv_forward": (ctypes.c_int, [_P, c_int32, c_int64, c_int32, _P, c_int32, _P, _P, _P, c_int32,
+                                        c_int64, c_int32, _P, c_int64, _P, _P, c_int32, _P, _P]),
     "tsc_to_dense": (ctypes.c_int, [_P, c_int32, _P, c_int64, c_int32, c_int32, _P, c_int32, _P, _P, _P]),
 }
 
@@ -181,6 +184,8 @@ def decode_status(bits: int) -> str:
         names.append("hash table ran out of probes")
     if bits & STATUS_OVERFLOW_FULL:
         names.append("duplicate-pair overflow list is full")
+    if bits & STATUS_WAIT_TIMEOUT:
+        names.append("a kernel timed out waiting on its own pipeline barrier")
     return "; ".join(names) or f"status 0x{bits:x}"
 
 

@@ -188,12 +188,16 @@ k_strided_mark(const int4* __restrict__ idx, int64_t n, GeoDev g, uint32_t* __re
       for (int kx = 0; kx < g.kW; ++kx, ++k) {
         const int cx = c.w + g.px - kx * g.dx;
         const bool v = active && vy && cx >= 0 && (cx % g.sx) == 0 && (cx / g.sx) < g.oW;
+        const unsigned b = __ballot_sync(kFullMask, v);
         if (v) {
+          // Lanes that hit the same bitmap word combine their bits; one atomic per word.
           const uint32_t lin = cell_key(c.x, oz, oy, cx / g.sx, g.oD, g.oH, g.oW);
-          atomicOr(&bitmap[lin >> 5], 1u << (lin & 31u));
+          const uint32_t word = lin >> 5;
+          const unsigned same = __match_any_sync(b, word);
+          const unsigned bits = __reduce_or_sync(same, 1u << (lin & 31u));
+          if (lane == __ffs(same) - 1) atomicOr(&bitmap[word], bits);
           any = true;
         }
-        const unsigned b = __ballot_sync(kFullMask, v);
         if (lane == 0 && b) atomicAdd(&s_cnt[k], static_cast<unsigned>(__popc(b)));
       }
     }
@@ -251,12 +255,13 @@ k_scan_tile_sums(U* __restrict__ sums, int64_t nblocks, unsigned long long* __re
   }
 }
 
-// Writes the exclusive prefix popcount of every bitmap word and the sorted
-// output coordinates (rank order == ascending cell key == the reference's
-// unique(sorted=True) order, decoded as indices.py:223-229).
+// Exclusive prefix popcount of every bitmap word: the rank of a set bit is
+// word_prefix[w] + popcount of the lower bits of its word, and rank order ==
+// ascending cell key == the reference's unique(sorted=True) order
+// (indices.py:219-229).
 __global__ void __launch_bounds__(kThreads)
-k_bitmap_emit(const uint4* __restrict__ bitmap, const uint32_t* __restrict__ tile_off,
-              uint32_t* __restrict__ word_prefix, GeoDev g, int4* __restrict__ out_idx, int64_t n_out) {
+k_bitmap_prefix(const uint4* __restrict__ bitmap, const uint32_t* __restrict__ tile_off,
+                uint32_t* __restrict__ word_prefix) {
   __shared__ uint32_t ws[32];
   const size_t w0 = static_cast<size_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
   const uint4 a = bitmap[w0 / 4], b = bitmap[w0 / 4 + 1];
@@ -275,15 +280,25 @@ k_bitmap_emit(const uint4* __restrict__ bitmap, const uint32_t* __restrict__ til
   uint4* wp = reinterpret_cast<uint4*>(word_prefix + w0);
   wp[0] = make_uint4(pre[0], pre[1], pre[2], pre[3]);
   wp[1] = make_uint4(pre[4], pre[5], pre[6], pre[7]);
+}
+
+// One thread per bitmap word: decode its set bits to coordinates at their
+// rank (a grid of one thread per word keeps sparse and dense grids alike
+// fully parallel).
+__global__ void __launch_bounds__(kThreads)
+k_bitmap_coords(const uint32_t* __restrict__ bitmap, const uint32_t* __restrict__ word_prefix,
+                int64_t nwords, GeoDev g, int4* __restrict__ out_idx, int64_t n_out) {
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (w >= nwords) return;
+  uint32_t wv = __ldg(&bitmap[w]);
+  if (wv == 0) return;
+  uint32_t r = __ldg(&word_prefix[w]);
   const unsigned oW = g.oW, oH = g.oH, oD = g.oD;
-#pragma unroll
-  for (int j = 0; j < kItems; ++j) {
-    uint32_t wv = words[j];
-    uint32_t r = pre[j];
+  {
     while (wv) {
       const int bit = __ffs(wv) - 1;
       wv &= wv - 1u;
-      const uint32_t lin = static_cast<uint32_t>((w0 + j) * 32u + bit);
+      const uint32_t lin = static_cast<uint32_t>(w * 32 + bit);
       const uint32_t x = lin % oW;
       uint32_t t = lin / oW;
       const uint32_t y = t % oH;
@@ -750,9 +765,13 @@ int tsc_strided_kmap_emit(const int32_t* indices, int64_t n_in, const tsc_geomet
   auto* prefix = reinterpret_cast<uint32_t*>(ws + w.off_prefix);
   auto* sums = reinterpret_cast<uint32_t*>(ws + w.off_sums);
   const GeoDev g = to_dev(*geo);
-  k_bitmap_emit<<<static_cast<unsigned>(w.nblocks), kThreads, 0, stream>>>(
-      reinterpret_cast<const uint4*>(bitmap), sums, prefix, g, reinterpret_cast<int4*>(out_indices), n_out);
-  TSC_LAUNCH_CHECK("k_bitmap_emit");
+  k_bitmap_prefix<<<static_cast<unsigned>(w.nblocks), kThreads, 0, stream>>>(
+      reinterpret_cast<const uint4*>(bitmap), sums, prefix);
+  TSC_LAUNCH_CHECK("k_bitmap_prefix");
+  const int64_t nwords = static_cast<int64_t>((w.nbits + 31) / 32);
+  k_bitmap_coords<<<static_cast<unsigned>(ceil_div(nwords, kThreads)), kThreads, 0, stream>>>(
+      bitmap, prefix, nwords, g, reinterpret_cast<int4*>(out_indices), n_out);
+  TSC_LAUNCH_CHECK("k_bitmap_coords");
   TSC_CUDA(cudaMemsetAsync(gather_map, 0xFF, sizeof(int32_t) * static_cast<size_t>(K) * n_out, stream));
   TSC_CUDA(cudaMemsetAsync(meta + TSC_META_N_OVERFLOW, 0, sizeof(int64_t), stream));
   const unsigned grid = static_cast<unsigned>(ceil_div(n_in, kThreads));

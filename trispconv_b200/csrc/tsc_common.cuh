@@ -59,10 +59,14 @@ __device__ __forceinline__ void raise_status(int64_t* status, long long bits) {
   atomicOr(reinterpret_cast<unsigned long long*>(status), static_cast<unsigned long long>(bits));
 }
 
-// Fibonacci hashing of a 32-bit linear cell key into a power-of-two table.
+// Slot of a 32-bit linear cell key in a power-of-two table (log2cap >= 8):
+// Fibonacci hashing of key >> 3, keeping the low 3 bits, so 8 cells that are
+// consecutive along x land in 8 consecutive slots (one or two cache sectors
+// for a warp querying neighbouring voxels).
 __device__ __forceinline__ uint32_t hash_slot(uint32_t key, int log2cap) {
-  return static_cast<uint32_t>((static_cast<unsigned long long>(key) * 0x9E3779B97F4A7C15ull) >>
-                               (64 - log2cap));
+  const uint32_t hi = static_cast<uint32_t>((static_cast<unsigned long long>(key >> 3) * 0x9E3779B97F4A7C15ull) >>
+                                            (64 - (log2cap - 3)));
+  return (hi << 3) | (key & 7u);
 }
 
 // Kernel offset decomposition, k = (kz*kH + ky)*kW + kx.

@@ -6,6 +6,7 @@ Triton path.
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -14,6 +15,29 @@ from trispconv_b200 import _lib as L
 from trispconv_b200.pytorch.indices import IndiceData, KernelMap, kmap_from_pairs
 
 SUPPORTED_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
+
+# TRISPCONV_B200_FORCE_SIMT=1 routes every conv to the CUDA-core kernel (A/B
+# measurements and tests of both kernels on the same inputs).
+_FORCE_FLAGS = L.CONV_FORCE_SIMT if os.environ.get("TRISPCONV_B200_FORCE_SIMT", "0") == "1" else 0
+# TRISPCONV_B200_TC=1 routes 16-bit convs with C_in % 8 == 0 to the tcgen05 kernel.
+if os.environ.get("TRISPCONV_B200_TC", "0") == "1":
+    _FORCE_FLAGS |= L.CONV_USE_TC
+
+
+def set_force_simt(on: bool) -> None:
+    global _FORCE_FLAGS
+    _FORCE_FLAGS = (_FORCE_FLAGS & ~L.CONV_FORCE_SIMT) | (L.CONV_FORCE_SIMT if on else 0)
+
+
+def set_tensor_memory_path(on: bool) -> None:
+    """Selects the tcgen05/TMEM kernel (on) or the mma.sync kernel (off) for
+    the 16-bit shapes both support."""
+    global _FORCE_FLAGS
+    _FORCE_FLAGS = (_FORCE_FLAGS & ~L.CONV_USE_TC) | (L.CONV_USE_TC if on else 0)
+
+
+def kernel_flags() -> int:
+    return _FORCE_FLAGS
 
 
 def kernel_map_for(indice_data: IndiceData, n_out: int, device: torch.device) -> KernelMap:
@@ -47,18 +71,25 @@ def conv_launch(features: torch.Tensor, weight: torch.Tensor, weight_layout: int
     if n_out == 0:
         return out
     feats = L.aligned(features, 16)
-    w = _as_dtype(weight, dtype)
-    b = None if bias is None else _as_dtype(bias.reshape(-1), dtype)
     if km is None:
-        gather = overflow = meta = None
+        gather = overflow = meta = order = None
         cap, k_vol = 0, 1
     else:
         gather, overflow, meta, cap, k_vol = km.gather, km.overflow, km.meta, km.overflow_cap, km.k_vol
+        order = km.row_order
+    if weight_layout == L.W_KCC and dtype != torch.float32:
+        # The tensor-core kernels read B as (C_out, K, C_in) rows: transpose the
+        # (K, C_in, C_out) weight once for this call.
+        weight = weight.reshape(k_vol, c_in, c_out).permute(2, 0, 1)
+        weight_layout = L.W_KRSC
+    w = _as_dtype(weight, dtype)
+    b = None if bias is None else _as_dtype(bias.reshape(-1), dtype)
     lib = L.load()
     rc = lib.tsc_conv_forward(feats.data_ptr() if n_in else None, L.DTYPE_CODE[dtype], n_in, c_in,
-                              w.data_ptr(), weight_layout, L.ptr(b), L.ptr(gather), k_vol, n_out, c_out,
-                              L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(),
-                              L.CONV_RELU if relu else 0, L.status_word(dev).data_ptr(), L.stream_ptr(dev))
+                              w.data_ptr(), weight_layout, L.ptr(b), L.ptr(gather), L.ptr(order), k_vol, n_out,
+                              c_out, L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(),
+                              (L.CONV_RELU if relu else 0) | _FORCE_FLAGS, L.status_word(dev).data_ptr(),
+                              L.stream_ptr(dev))
     L.check(rc, "tsc_conv_forward")
     if L.EAGER_CHECKS:
         L.check_device_status(dev)

@@ -48,15 +48,17 @@ class KernelMap:
     meta     int64 [8 + K]: counts written by the builders (pair_num at 8..).
     pair_map / pair_mode / pair_remap: how tsc_pairs_materialize recreates the
              reference-ordered pair lists.
+    row_order int32 [n_out] or None: order in which the conv kernel groups
+             output rows into tiles (does not change results).
     """
 
     __slots__ = ("k_vol", "n_in", "n_out", "gather", "scatter", "overflow", "overflow_cap", "meta",
-                 "pair_map", "pair_mode", "pair_remap", "n_part", "device")
+                 "pair_map", "pair_mode", "pair_remap", "n_part", "device", "row_order")
 
     def __init__(self, k_vol: int, n_in: int, n_out: int, gather: Optional[torch.Tensor],
                  meta: Optional[torch.Tensor], device: torch.device, *, scatter=None, overflow=None,
                  overflow_cap: int = 0, pair_map=None, pair_mode: int = 0, pair_remap=None,
-                 n_part: Optional[int] = None):
+                 n_part: Optional[int] = None, row_order: Optional[torch.Tensor] = None):
         self.k_vol = k_vol
         self.n_in = n_in
         self.n_out = n_out
@@ -70,6 +72,7 @@ class KernelMap:
         self.pair_remap = pair_remap
         self.n_part = n_part
         self.device = device
+        self.row_order = row_order
 
 
 class IndiceData:

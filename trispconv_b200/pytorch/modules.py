@@ -216,6 +216,12 @@ class SparseSequential(SparseModule):
         for key, module in kwargs.items():
             self.add_module(key, module)
 
+    def __len__(self) -> int:
+        return len(self._modules)
+
+    def __getitem__(self, idx: int) -> nn.Module:
+        return list(self._modules.values())[idx]
+
     def forward(self, x: Union[SparseConvTensor, torch.Tensor]) -> Union[SparseConvTensor, torch.Tensor]:
         mods = list(self.children())
         i = 0
