@@ -19,6 +19,13 @@ def _cloud(rng, shape, n):
     return np.stack([np.zeros(n), z, y, x], 1).astype(np.int32)
 
 
+@pytest.fixture(params=["persistent", "one_tile_per_cta"])
+def tc_variant(request):
+    Fn.set_tc_simple(request.param != "persistent")
+    yield request.param
+    Fn.set_tc_simple(False)
+
+
 def _run_both(m, x_fn):
     Fn.set_tensor_memory_path(True)
     try:
@@ -46,7 +53,7 @@ def _assert_same(a, b, dtype, what):
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
 @pytest.mark.parametrize("cin,cout", [(64, 64), (16, 32), (32, 64), (64, 128), (128, 128), (128, 256),
                                       (256, 256), (96, 40), (8, 24), (192, 512)])
-def test_tc_matches_cuda_core(cuda, dtype, cin, cout):
+def test_tc_matches_cuda_core(cuda, tc_variant, dtype, cin, cout):
     rng = np.random.default_rng(cin * 31 + cout)
     shape = (18, 20, 22)
     idx = torch.from_numpy(_cloud(rng, shape, 3001)).to(cuda)  # not a multiple of 128 rows
@@ -61,7 +68,7 @@ def test_tc_matches_cuda_core(cuda, dtype, cin, cout):
         _assert_same(a, b, dtype, f"{kind} {cin}->{cout}")
 
 
-def test_tc_vs_oracle_and_relu(cuda):
+def test_tc_vs_oracle_and_relu(cuda, tc_variant):
     rng = np.random.default_rng(2)
     shape = (16, 16, 16)
     idx = _cloud(rng, shape, 2000)
@@ -90,7 +97,7 @@ def test_tc_vs_oracle_and_relu(cuda):
     _lib.check_device_status(cuda)
 
 
-def test_tc_duplicates_use_overflow(cuda):
+def test_tc_duplicates_use_overflow(cuda, tc_variant):
     rng = np.random.default_rng(4)
     base = rng.integers(0, 10, (300, 3))
     xyz = np.concatenate([base, base[:120]])
@@ -102,7 +109,7 @@ def test_tc_duplicates_use_overflow(cuda):
     _assert_same(a, b, torch.float16, "duplicates")
 
 
-def test_tc_one_by_one_and_empty_tiles(cuda):
+def test_tc_one_by_one_and_empty_tiles(cuda, tc_variant):
     rng = np.random.default_rng(5)
     shape = (8, 8, 8)
     idx = torch.from_numpy(_cloud(rng, shape, 200)).to(cuda)
@@ -116,3 +123,23 @@ def test_tc_one_by_one_and_empty_tiles(cuda):
     fa = f[:3].contiguous()
     a, b = _run_both(m3, lambda: spconv.SparseConvTensor(fa, far, shape, 1))
     _assert_same(a, b, torch.float16, "isolated")
+
+
+@pytest.mark.parametrize("cin,cout", [(64, 64), (32, 32), (128, 128), (64, 256)])
+def test_tc_many_tiles_per_cta(cuda, cin, cout):
+    """~330k rows = ~1300 tiles of 256: every persistent CTA walks several
+    tiles through both TMEM accumulator buffers and around the stage ring."""
+    rng = np.random.default_rng(cin + cout)
+    shape = (70, 70, 70)
+    n = 330_000
+    idx = torch.from_numpy(_cloud(rng, shape, n)).to(cuda)
+    f = torch.from_numpy(rng.standard_normal((n, cin)).astype(np.float32)).to(cuda).half()
+    m = spconv.SubMConv3d(cin, cout, 3).to(cuda).half()
+    with torch.no_grad():
+        m.bias.normal_(0, 0.1)
+    Fn.set_tc_simple(False)
+    a, b = _run_both(m, lambda: spconv.SparseConvTensor(f, idx, shape, 1))
+    _assert_same(a, b, torch.float16, f"many tiles {cin}->{cout}")
+    from trispconv_b200 import _lib
+
+    _lib.check_device_status(cuda)

@@ -40,9 +40,15 @@ struct Cfg {
   static constexpr int RING = (TN <= 64 ? 96 : 192) * 1024;
   static constexpr int NS = RING / STAGE > 12 ? 12 : (RING / STAGE < 2 ? 2 : RING / STAGE);
   static constexpr int PIPE = NS * STAGE;
-  // control block after the ring: barriers (full[NS], empty[NS], done),
-  // tmem address, flags, active offsets, out rows, gather rows [K][BM]
-  static constexpr int CTRL = 256;
+  // control block after the ring: barriers full[NS] @0, empty[NS] @8*NS,
+  // done @16*NS, then tmem address, abort flag, number of active offsets;
+  // followed by active offsets, out rows and gather rows [K][BM]
+  static constexpr int OFF_EMPTY = 8 * NS;
+  static constexpr int OFF_DONE = 16 * NS;
+  static constexpr int OFF_TMEM = OFF_DONE + 8;
+  static constexpr int OFF_ABORT = OFF_TMEM + 4;
+  static constexpr int OFF_NACTIVE = OFF_ABORT + 4;
+  static constexpr int CTRL = (OFF_NACTIVE + 4 + 127) / 128 * 128;
   static constexpr int TOTAL_FIXED = 1024 /*alignment slack*/ + PIPE + CTRL + (KMAX + BM) * 4;
   static constexpr int TMEM_COLS = TN < 32 ? 32 : TN;
   static constexpr int SWZ_MODE = KC == 64 ? 2 : (KC == 32 ? 4 : 6);  // UMMA layout type
@@ -73,13 +79,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: false on timeout or when another role aborted.
+// Bounded wait: false on timeout (kWaitNs after the wait began) or when
+// another role aborted.  The `deadline` argument is unused and kept for the
+// call sites' symmetry.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long deadline,
                                           volatile int* abort_flag, int64_t* status) {
+  (void)deadline;
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long limit = globaltimer() + kWaitNs;
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() > deadline) {
+    if (globaltimer() > limit) {
       raise_status(status, TSC_STATUS_WAIT_TIMEOUT);
       *abort_flag = 1;
       return false;
@@ -177,14 +188,13 @@ k_conv_tc(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__
   const uint32_t ring_u32 = raw_u32 + pad;
   unsigned char* ctrl = ring + C::PIPE;
   const uint32_t ctrl_u32 = ring_u32 + C::PIPE;
-  // control block layout (bytes): full[NS] @0, empty[NS] @64, done @128,
-  // tmem addr @136, abort @140, n_active @144, any_rows @148
+  static_assert(C::OFF_NACTIVE + 4 <= C::CTRL, "control block overflow");
   const uint32_t bar_full = ctrl_u32;
-  const uint32_t bar_empty = ctrl_u32 + 64;
-  const uint32_t bar_done = ctrl_u32 + 128;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(ctrl + 136);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(ctrl + 140);
-  int* s_nactive = reinterpret_cast<int*>(ctrl + 144);
+  const uint32_t bar_empty = ctrl_u32 + C::OFF_EMPTY;
+  const uint32_t bar_done = ctrl_u32 + C::OFF_DONE;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(ctrl + C::OFF_TMEM);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(ctrl + C::OFF_ABORT);
+  int* s_nactive = reinterpret_cast<int*>(ctrl + C::OFF_NACTIVE);
   int32_t* s_klist = reinterpret_cast<int32_t*>(ctrl + C::CTRL);
   int32_t* s_orow = s_klist + KMAX;
   int32_t* s_rows = s_orow + BM;  // [K][BM]
@@ -214,7 +224,7 @@ k_conv_tc(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__
   if (warp == 4) {
     __syncwarp();
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     static_cast<uint32_t>(ctrl_u32 + 136)),
+                     static_cast<uint32_t>(ctrl_u32 + C::OFF_TMEM)),
                  "r"(C::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }

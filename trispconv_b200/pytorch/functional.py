@@ -36,6 +36,12 @@ def set_tensor_memory_path(on: bool) -> None:
     _FORCE_FLAGS = (_FORCE_FLAGS & ~L.CONV_USE_TC) | (L.CONV_USE_TC if on else 0)
 
 
+def set_tc_simple(on: bool) -> None:
+    """Selects the one-tile-per-CTA tcgen05 kernel instead of the persistent one."""
+    global _FORCE_FLAGS
+    _FORCE_FLAGS = (_FORCE_FLAGS & ~L.CONV_TC_SIMPLE) | (L.CONV_TC_SIMPLE if on else 0)
+
+
 def kernel_flags() -> int:
     return _FORCE_FLAGS
 
