@@ -51,14 +51,22 @@ def build(verbose: bool = False, force: bool = False) -> Path:
             return LIB
     BUILD_DIR.mkdir(exist_ok=True)
     nvcc = _nvcc()
-    objs = []
-    for src in srcs:
+
+    def compile_one(src: Path):
         obj = BUILD_DIR / (src.stem + ".o")
         cmd = [nvcc, *GENCODE, *NVCC_FLAGS, "-I", str(ROOT / "include"), "-I", str(CSRC),
                "-c", str(src), "-o", str(obj)]
         res = subprocess.run(cmd, capture_output=True, text=True)
-        log = BUILD_DIR / (src.stem + ".ptxas.txt")
-        log.write_text(res.stdout + res.stderr)
+        (BUILD_DIR / (src.stem + ".ptxas.txt")).write_text(res.stdout + res.stderr)
+        return src, obj, res
+
+    from concurrent.futures import ThreadPoolExecutor
+
+    workers = max(1, min(len(srcs), os.cpu_count() or 1))
+    with ThreadPoolExecutor(max_workers=workers) as pool:
+        results = list(pool.map(compile_one, srcs))
+    objs = []
+    for src, obj, res in results:
         if res.returncode != 0:
             sys.stderr.write(res.stdout + res.stderr)
             raise RuntimeError(f"nvcc failed on {src.name}")

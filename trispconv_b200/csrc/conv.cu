@@ -7,9 +7,7 @@
 // once with bias (and optionally ReLU) fused; no atomics, no zero-fill pass.
 #include <cstdint>
 
-#include "conv_mma.cuh"
-#include "conv_tc.cuh"
-#include "conv_tcp.cuh"
+#include "conv_launch.h"
 #include "tsc_common.cuh"
 
 namespace tsc {
@@ -177,200 +175,6 @@ int launch_simt(const void* F, int64_t n_in, int c_in, const void* W, int w_krsc
   return TSC_OK;
 }
 
-// ---- tensor-core (mma.sync) path -------------------------------------------
-
-template <typename T, int TN, int KC, int CH>
-int launch_mma_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
-                   const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                   const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
-  using C = mma::Cfg<TN, KC>;
-  auto kern = mma::k_conv_mma<T, TN, KC, CH>;
-  static unsigned long long configured = 0;  // one bit per device
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
-    TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL));
-    configured |= 1ull << (dev & 63);
-  }
-  dim3 grid(static_cast<unsigned>(ceil_div(n_out, mma::BM)), static_cast<unsigned>(ceil_div(c_out, TN)));
-  kern<<<grid, mma::NT, C::bytes(K), stream>>>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap,
-                                               meta, out, flags, status);
-  TSC_LAUNCH_CHECK("k_conv_mma");
-  return TSC_OK;
-}
-
-// ---- tcgen05 path ------------------------------------------------------------
-
-template <typename T, int TN, int KC>
-int launch_tc_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
-                  const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                  const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
-  using C = tc::Cfg<TN, KC>;
-  auto kern = tc::k_conv_tc<T, TN, KC>;
-  const int smem = C::TOTAL_FIXED + K * tc::BM * 4;
-  static unsigned long long configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
-    TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  C::TOTAL_FIXED + tc::KMAX * tc::BM * 4));
-    configured |= 1ull << (dev & 63);
-  }
-  dim3 grid(static_cast<unsigned>(ceil_div(n_out, tc::BM)), static_cast<unsigned>(ceil_div(c_out, TN)));
-  kern<<<grid, tc::NT, smem, stream>>>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
-                                       out, flags, status);
-  TSC_LAUNCH_CHECK("k_conv_tc");
-  return TSC_OK;
-}
-
-template <typename T, int TN>
-int launch_tc_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
-                 const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                 const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
-  if (c_in <= 16)
-    return launch_tc_cfg<T, TN, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                    flags, status, stream);
-  if (c_in <= 32)
-    return launch_tc_cfg<T, TN, 32>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                    flags, status, stream);
-  return launch_tc_cfg<T, TN, 64>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                  flags, status, stream);
-}
-
-// ---- persistent tcgen05 path ---------------------------------------------------
-
-template <typename T, int TN, int KC>
-int launch_tcp_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
-                   const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                   const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
-  using C = tcp::Cfg<TN, KC>;
-  auto kern = tcp::k_conv_tcp<T, TN, KC>;
-  static unsigned long long configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
-    TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL));
-    configured |= 1ull << (dev & 63);
-  }
-  const int64_t tiles = ceil_div(n_out, tcp::BMT) * ceil_div(c_out, TN);
-  const int64_t grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<static_cast<unsigned>(grid), tcp::NT, C::TOTAL, stream>>>(f, n_in, c_in, w, bias, gmap, perm, K, n_out,
-                                                                  c_out, ovf, ovf_cap, meta, out, flags, status);
-  TSC_LAUNCH_CHECK("k_conv_tcp");
-  return TSC_OK;
-}
-
-template <typename T, int TN>
-int launch_tcp_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
-                  const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                  const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
-  if (c_in <= 16)
-    return launch_tcp_cfg<T, TN, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                     flags, status, stream);
-  if (c_in <= 32)
-    return launch_tcp_cfg<T, TN, 32>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                     flags, status, stream);
-  return launch_tcp_cfg<T, TN, 64>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                   flags, status, stream);
-}
-
-template <typename T>
-int launch_tcp(const void* F, int64_t n_in, int c_in, const void* W, const void* bias, const int32_t* gmap,
-               const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-               const int64_t* meta, void* out, int flags, int64_t* status, cudaStream_t stream) {
-  const T* f = static_cast<const T*>(F);
-  const T* w = static_cast<const T*>(W);
-  const T* b = static_cast<const T*>(bias);
-  T* o = static_cast<T*>(out);
-  if (c_out <= 32)
-    return launch_tcp_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                status, stream);
-  if (c_out <= 64)
-    return launch_tcp_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                status, stream);
-  if (c_out <= 128)
-    return launch_tcp_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                 status, stream);
-  return launch_tcp_tn<T, 256>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                               status, stream);
-}
-
-// tcgen05 path: 16-bit types, KRSC weights, C_in % 8 == 0, C_out % 8 == 0, K <= 64.
-bool tc_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
-  if (dtype != TSC_F16 && dtype != TSC_BF16) return false;
-  return w_krsc && K <= tc::KMAX && c_in % 8 == 0 && c_out % 8 == 0;
-}
-
-template <typename T>
-int launch_tc(const void* F, int64_t n_in, int c_in, const void* W, const void* bias, const int32_t* gmap,
-              const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-              const int64_t* meta, void* out, int flags, int64_t* status, cudaStream_t stream) {
-  const T* f = static_cast<const T*>(F);
-  const T* w = static_cast<const T*>(W);
-  const T* b = static_cast<const T*>(bias);
-  T* o = static_cast<T*>(out);
-  if (c_out <= 32)
-    return launch_tc_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                               status, stream);
-  if (c_out <= 64)
-    return launch_tc_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                               status, stream);
-  if (c_out <= 128)
-    return launch_tc_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                status, stream);
-  return launch_tc_tn<T, 256>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                              status, stream);
-}
-
-template <typename T, int TN>
-int launch_mma_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
-                  const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                  const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
-  if (c_in <= 16) {
-    if (c_in % 8 == 0)
-      return launch_mma_cfg<T, TN, 16, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
-                                           out, flags, status, stream);
-    return launch_mma_cfg<T, TN, 16, 8>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
-                                        out, flags, status, stream);
-  }
-  if (c_in <= 32)
-    return launch_mma_cfg<T, TN, 32, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
-                                         out, flags, status, stream);
-  return launch_mma_cfg<T, TN, 64, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                       flags, status, stream);
-}
-
-// Shapes the tensor-core kernel handles: 16-bit types, KRSC weights,
-// C_in a multiple of 8 (or of 4 up to 16), C_out a multiple of 8, K <= 64.
-bool mma_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
-  if (dtype != TSC_F16 && dtype != TSC_BF16) return false;
-  if (!w_krsc || K > mma::KMAX || c_out % 8 != 0) return false;
-  if (c_in % 8 == 0) return true;
-  return c_in % 4 == 0 && c_in <= 16;
-}
-
-template <typename T>
-int launch_mma(const void* F, int64_t n_in, int c_in, const void* W, const void* bias, const int32_t* gmap,
-               const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-               const int64_t* meta, void* out, int flags, int64_t* status, cudaStream_t stream) {
-  const T* f = static_cast<const T*>(F);
-  const T* w = static_cast<const T*>(W);
-  const T* b = static_cast<const T*>(bias);
-  T* o = static_cast<T*>(out);
-  if (c_out <= 16)
-    return launch_mma_tn<T, 16>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                status, stream);
-  if (c_out <= 32)
-    return launch_mma_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                status, stream);
-  if (c_out <= 64)
-    return launch_mma_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                status, stream);
-  return launch_mma_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                               status, stream);
-}
-
-// Dense scatter for SparseConvTensor.dense().
 template <typename T>
 __global__ void __launch_bounds__(256)
 k_to_dense(const T* __restrict__ F, const int4* __restrict__ idx, int64_t n, int C, int B, int D, int H,
@@ -448,28 +252,16 @@ int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t 
                 "overflow list needs its meta buffer");
   const int w_krsc = weight_layout == TSC_W_KRSC;
   const bool force_simt = (flags & TSC_CONV_FORCE_SIMT) != 0;
-  if (!force_simt && (flags & TSC_CONV_USE_TC) != 0 && tc_eligible(dtype, w_krsc, c_in, c_out, k_vol) &&
-      n_in > 0 && k_vol <= tcp::KMAX && (flags & TSC_CONV_TC_SIMPLE) == 0) {
-    if (dtype == TSC_F16)
-      return launch_tcp<__half>(features, n_in, c_in, weight, bias, gather_map, row_order, k_vol, n_out, c_out,
-                                overflow, overflow_cap, meta, out, flags, status, stream);
-    return launch_tcp<__nv_bfloat16>(features, n_in, c_in, weight, bias, gather_map, row_order, k_vol, n_out,
-                                     c_out, overflow, overflow_cap, meta, out, flags, status, stream);
-  }
+  const ConvArgs a{features, n_in, c_in, weight, bias, gather_map, row_order, k_vol, n_out, c_out,
+                   overflow, overflow_cap, meta, out, flags, status, stream};
+  const bool f16 = dtype == TSC_F16;
   if (!force_simt && (flags & TSC_CONV_USE_TC) != 0 && tc_eligible(dtype, w_krsc, c_in, c_out, k_vol)) {
-    if (dtype == TSC_F16)
-      return launch_tc<__half>(features, n_in, c_in, weight, bias, gather_map, row_order, k_vol, n_out, c_out,
-                               overflow, overflow_cap, meta, out, flags, status, stream);
-    return launch_tc<__nv_bfloat16>(features, n_in, c_in, weight, bias, gather_map, row_order, k_vol, n_out, c_out,
-                                    overflow, overflow_cap, meta, out, flags, status, stream);
+    if (n_in > 0 && k_vol <= kPersistentKMax && (flags & TSC_CONV_TC_SIMPLE) == 0)
+      return f16 ? launch_tcp_f16(a) : launch_tcp_bf16(a);
+    return f16 ? launch_tc_f16(a) : launch_tc_bf16(a);
   }
-  if (!force_simt && mma_eligible(dtype, w_krsc, c_in, c_out, k_vol)) {
-    if (dtype == TSC_F16)
-      return launch_mma<__half>(features, n_in, c_in, weight, bias, gather_map, row_order, k_vol, n_out, c_out,
-                                overflow, overflow_cap, meta, out, flags, status, stream);
-    return launch_mma<__nv_bfloat16>(features, n_in, c_in, weight, bias, gather_map, row_order, k_vol, n_out,
-                                     c_out, overflow, overflow_cap, meta, out, flags, status, stream);
-  }
+  if (!force_simt && mma_eligible(dtype, w_krsc, c_in, c_out, k_vol))
+    return f16 ? launch_mma_f16(a) : launch_mma_bf16(a);
   TSC_CHECK_ARG(row_order == nullptr, "row_order is only supported by the tensor-core path");
   switch (dtype) {
     case TSC_F32:

@@ -1,0 +1,60 @@
+// Launch entry points of the tensor-core convolution kernels, one per kernel
+// family and element type (each defined in its own conv_launch_*.cu so the
+// heavy template instantiations compile in parallel).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "trispconv_b200.h"
+
+namespace tsc {
+
+struct ConvArgs {
+  const void* features;
+  int64_t n_in;
+  int c_in;
+  const void* weight;  // KRSC (C_out, K, C_in)
+  const void* bias;
+  const int32_t* gather_map;
+  const int32_t* row_order;
+  int k_vol;
+  int64_t n_out;
+  int c_out;
+  const int32_t* overflow;
+  int64_t overflow_cap;
+  const int64_t* meta;
+  void* out;
+  int flags;
+  int64_t* status;
+  cudaStream_t stream;
+};
+
+// Largest kernel volumes the tensor-core kernels take (gather-map slice in
+// shared memory; one 32-bit active-offset mask for the persistent kernel).
+constexpr int kMmaKMax = 64;
+constexpr int kPersistentKMax = 27;
+
+// mma.sync path: 16-bit types, KRSC weights, C_in % 8 == 0 (or C_in % 4 == 0
+// and C_in <= 16), C_out % 8 == 0.
+inline bool mma_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
+  if (dtype != TSC_F16 && dtype != TSC_BF16) return false;
+  if (!w_krsc || K > kMmaKMax || c_out % 8 != 0) return false;
+  if (c_in % 8 == 0) return true;
+  return c_in % 4 == 0 && c_in <= 16;
+}
+
+// tcgen05 paths: 16-bit types, KRSC weights, C_in % 8 == 0, C_out % 8 == 0.
+inline bool tc_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
+  if (dtype != TSC_F16 && dtype != TSC_BF16) return false;
+  return w_krsc && K <= kMmaKMax && c_in % 8 == 0 && c_out % 8 == 0;
+}
+
+int launch_mma_f16(const ConvArgs& a);
+int launch_mma_bf16(const ConvArgs& a);
+int launch_tc_f16(const ConvArgs& a);
+int launch_tc_bf16(const ConvArgs& a);
+int launch_tcp_f16(const ConvArgs& a);
+int launch_tcp_bf16(const ConvArgs& a);
+
+}  // namespace tsc

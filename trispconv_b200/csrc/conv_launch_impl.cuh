@@ -1,0 +1,277 @@
+// Template launchers of the tensor-core conv kernels.  Each
+// conv_launch_*.cu translation unit instantiates one kernel family for one
+// element type, so the library compiles in parallel.
+#pragma once
+
+#include <cuda.h>
+#include <type_traits>
+
+#include "conv_launch.h"
+#include "conv_mma.cuh"
+#include "conv_tc.cuh"
+#include "conv_tcp.cuh"
+#include "tsc_common.cuh"
+
+namespace tsc {
+namespace detail {
+
+static_assert(tcp::KMAX == kPersistentKMax, "persistent kernel K limit");
+static_assert(mma::KMAX == kMmaKMax && tc::KMAX == kMmaKMax, "kernel K limits");
+
+// ---- tensor-core (mma.sync) path -------------------------------------------
+
+template <typename T, int TN, int KC, int CH>
+int launch_mma_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
+                   const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
+                   const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+  using C = mma::Cfg<TN, KC>;
+  auto kern = mma::k_conv_mma<T, TN, KC, CH>;
+  static unsigned long long configured = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL));
+    configured |= 1ull << (dev & 63);
+  }
+  dim3 grid(static_cast<unsigned>(ceil_div(n_out, mma::BM)), static_cast<unsigned>(ceil_div(c_out, TN)));
+  kern<<<grid, mma::NT, C::bytes(K), stream>>>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap,
+                                               meta, out, flags, status);
+  TSC_LAUNCH_CHECK("k_conv_mma");
+  return TSC_OK;
+}
+
+// ---- tcgen05 path ------------------------------------------------------------
+
+template <typename T, int TN, int KC>
+int launch_tc_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
+                  const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
+                  const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+  using C = tc::Cfg<TN, KC>;
+  auto kern = tc::k_conv_tc<T, TN, KC>;
+  const int smem = C::TOTAL_FIXED + K * tc::BM * 4;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  C::TOTAL_FIXED + tc::KMAX * tc::BM * 4));
+    configured |= 1ull << (dev & 63);
+  }
+  dim3 grid(static_cast<unsigned>(ceil_div(n_out, tc::BM)), static_cast<unsigned>(ceil_div(c_out, TN)));
+  kern<<<grid, tc::NT, smem, stream>>>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
+                                       out, flags, status);
+  TSC_LAUNCH_CHECK("k_conv_tc");
+  return TSC_OK;
+}
+
+template <typename T, int TN>
+int launch_tc_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
+                 const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
+                 const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+  if (c_in <= 16)
+    return launch_tc_cfg<T, TN, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
+                                    flags, status, stream);
+  if (c_in <= 32)
+    return launch_tc_cfg<T, TN, 32>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
+                                    flags, status, stream);
+  return launch_tc_cfg<T, TN, 64>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
+                                  flags, status, stream);
+}
+
+// ---- persistent tcgen05 path ---------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the
+// library does not link libcuda directly).
+inline int encode_fn(EncodeTiledFn* out) {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || p == nullptr) {
+      set_error("cuTensorMapEncodeTiled is not available from the driver");
+      return TSC_ERR_CUDA;
+    }
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  *out = fn;
+  return TSC_OK;
+}
+
+template <typename T>
+constexpr CUtensorMapDataType tma_dtype() {
+  return std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+template <int KC>
+constexpr CUtensorMapSwizzle tma_swizzle() {
+  return KC == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : (KC == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
+// Features [n_in][c_in] as a 2-D tensor {c_in, n_in}, box {KC, 1} (gather4),
+// and KRSC weights [c_out][K][c_in] as a 3-D tensor {c_in, K, c_out}, box
+// {KC, 1, TN}; both swizzled like the UMMA K-major operand tiles, zero fill
+// outside the tensor.
+template <typename T, int TN, int KC>
+int encode_maps(const T* f, int64_t n_in, int c_in, const T* w, int K, int c_out, CUtensorMap* mf, CUtensorMap* mw) {
+  EncodeTiledFn enc;
+  int rc = encode_fn(&enc);
+  if (rc != TSC_OK) return rc;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(c_in), static_cast<cuuint64_t>(n_in)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(c_in) * sizeof(T)};
+    cuuint32_t box[2] = {KC, 1};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(mf, tma_dtype<T>(), 2, const_cast<T*>(f), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     tma_swizzle<KC>(), CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("cuTensorMapEncodeTiled(features) failed with %d", static_cast<int>(r));
+      return TSC_ERR_CUDA;
+    }
+  }
+  {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(c_in), static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(c_out)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(c_in) * sizeof(T),
+                             static_cast<cuuint64_t>(K) * c_in * sizeof(T)};
+    cuuint32_t box[3] = {KC, 1, TN};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = enc(mw, tma_dtype<T>(), 3, const_cast<T*>(w), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     tma_swizzle<KC>(), CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("cuTensorMapEncodeTiled(weights) failed with %d", static_cast<int>(r));
+      return TSC_ERR_CUDA;
+    }
+  }
+  return TSC_OK;
+}
+
+template <typename T, int TN, int KC>
+int launch_tcp_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
+                   const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
+                   const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+  using C = tcp::Cfg<TN, KC>;
+  auto kern = tcp::k_conv_tcp<T, TN, KC>;
+  CUtensorMap mf, mw;
+  int rc = encode_maps<T, TN, KC>(f, n_in, c_in, w, K, c_out, &mf, &mw);
+  if (rc != TSC_OK) return rc;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL));
+    configured |= 1ull << (dev & 63);
+  }
+  const int64_t tiles = ceil_div(n_out, tcp::BMT) * ceil_div(c_out, TN);
+  const int64_t grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<static_cast<unsigned>(grid), tcp::NT, C::TOTAL, stream>>>(mf, mw, f, n_in, c_in, w, bias, gmap, perm, K,
+                                                                  n_out, c_out, ovf, ovf_cap, meta, out, flags,
+                                                                  status);
+  TSC_LAUNCH_CHECK("k_conv_tcp");
+  return TSC_OK;
+}
+
+template <typename T, int TN>
+int launch_tcp_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
+                  const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
+                  const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+  if (c_in <= 16)
+    return launch_tcp_cfg<T, TN, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
+                                     flags, status, stream);
+  if (c_in <= 32)
+    return launch_tcp_cfg<T, TN, 32>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
+                                     flags, status, stream);
+  return launch_tcp_cfg<T, TN, 64>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
+                                   flags, status, stream);
+}
+
+template <typename T>
+int launch_tcp(const void* F, int64_t n_in, int c_in, const void* W, const void* bias, const int32_t* gmap,
+               const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
+               const int64_t* meta, void* out, int flags, int64_t* status, cudaStream_t stream) {
+  const T* f = static_cast<const T*>(F);
+  const T* w = static_cast<const T*>(W);
+  const T* b = static_cast<const T*>(bias);
+  T* o = static_cast<T*>(out);
+  if (c_out <= 32)
+    return launch_tcp_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                                status, stream);
+  if (c_out <= 64)
+    return launch_tcp_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                                status, stream);
+  if (c_out <= 128)
+    return launch_tcp_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                                 status, stream);
+  return launch_tcp_tn<T, 256>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                               status, stream);
+}
+
+
+template <typename T>
+int launch_tc(const void* F, int64_t n_in, int c_in, const void* W, const void* bias, const int32_t* gmap,
+              const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
+              const int64_t* meta, void* out, int flags, int64_t* status, cudaStream_t stream) {
+  const T* f = static_cast<const T*>(F);
+  const T* w = static_cast<const T*>(W);
+  const T* b = static_cast<const T*>(bias);
+  T* o = static_cast<T*>(out);
+  if (c_out <= 32)
+    return launch_tc_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                               status, stream);
+  if (c_out <= 64)
+    return launch_tc_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                               status, stream);
+  if (c_out <= 128)
+    return launch_tc_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                                status, stream);
+  return launch_tc_tn<T, 256>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                              status, stream);
+}
+
+template <typename T, int TN>
+int launch_mma_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
+                  const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
+                  const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+  if (c_in <= 16) {
+    if (c_in % 8 == 0)
+      return launch_mma_cfg<T, TN, 16, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
+                                           out, flags, status, stream);
+    return launch_mma_cfg<T, TN, 16, 8>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
+                                        out, flags, status, stream);
+  }
+  if (c_in <= 32)
+    return launch_mma_cfg<T, TN, 32, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
+                                         out, flags, status, stream);
+  return launch_mma_cfg<T, TN, 64, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
+                                       flags, status, stream);
+}
+
+
+template <typename T>
+int launch_mma(const void* F, int64_t n_in, int c_in, const void* W, const void* bias, const int32_t* gmap,
+               const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
+               const int64_t* meta, void* out, int flags, int64_t* status, cudaStream_t stream) {
+  const T* f = static_cast<const T*>(F);
+  const T* w = static_cast<const T*>(W);
+  const T* b = static_cast<const T*>(bias);
+  T* o = static_cast<T*>(out);
+  if (c_out <= 16)
+    return launch_mma_tn<T, 16>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                                status, stream);
+  if (c_out <= 32)
+    return launch_mma_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                                status, stream);
+  if (c_out <= 64)
+    return launch_mma_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                                status, stream);
+  return launch_mma_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                               status, stream);
+}
+
+// Dense scatter for SparseConvTensor.dense().
+
+}  // namespace detail
+}  // namespace tsc

@@ -30,6 +30,7 @@ constexpr int NPROD = 128;          // producer / epilogue threads (warps 0-3)
 constexpr int NT = NPROD + 32;      // + MMA warp
 constexpr int KMAX = 64;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per kernel
+constexpr long long kWaitCycles = 4000000000ll;        // bounded barrier waits (~2 s)
 
 template <int TN, int KC>
 struct Cfg {
@@ -86,11 +87,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
                                           volatile int* abort_flag, int64_t* status) {
   (void)deadline;
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long limit = globaltimer() + kWaitNs;
+  // SM cycle counter (cheap to read, unlike %globaltimer): ~2 s at 2 GHz.
+  const long long start = clock64();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() > limit) {
+    if (clock64() - start > kWaitCycles) {
       raise_status(status, TSC_STATUS_WAIT_TIMEOUT);
       *abort_flag = 1;
       return false;
@@ -149,6 +151,27 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, unsigned long long a, 
       ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+
+// Same, with a per-row disable mask: D rows (TMEM lanes) whose bit is set in
+// {m0..m3} (lane i -> m[i / 32] bit i % 32) are left unchanged.
+__device__ __forceinline__ void umma_f16_masked(uint32_t tmem_d, unsigned long long a, unsigned long long b,
+                                                uint32_t idesc, uint32_t accumulate, uint32_t m0, uint32_t m1,
+                                                uint32_t m2, uint32_t m3) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p; }"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32_zero(uint32_t taddr) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)

@@ -22,6 +22,8 @@
 // one tile run under the MMAs of the next.  All mbarrier waits are bounded.
 #pragma once
 
+#include <cuda.h>
+
 #include "conv_tc.cuh"
 
 namespace tsc {
@@ -32,7 +34,37 @@ constexpr int HALF = 128;      // rows per UMMA
 constexpr int NPROD = 128;     // producer threads
 constexpr int NEPI = 128;      // epilogue threads
 constexpr int NT = NPROD + 32 + NEPI;
-constexpr int KMAX = 32;       // offsets per map (one 32-bit active mask)
+constexpr int KMAX = 27;       // offsets per map (3x3x3 and smaller; 32-bit active mask)
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(mma::smem_u32(dst)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// TMA gather of 4 feature rows (y0..y3; an out-of-range row index reads the
+// zero fill) x box-width channels starting at channel x, into 4 consecutive
+// swizzled shared-memory rows at dst.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* tmap, int x, int y0, int y1, int y2,
+                                            int y3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(bar)
+      : "memory");
+}
+
+// TMA tile load of the weight slice W[n0:n0+TN, k, c0:c0+KC] (KRSC viewed as
+// a 3-D tensor {C_in, K, C_out}); out-of-range channels read the zero fill.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tmap, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
 
 template <int TN, int KC>
 struct Cfg {
@@ -41,7 +73,7 @@ struct Cfg {
   static constexpr int A_BYTES = BMT * KC * 2;
   static constexpr int B_BYTES = TN * KC * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int RING_TARGET = 168 * 1024;
+  static constexpr int RING_TARGET = 160 * 1024;
   static constexpr int NS = RING_TARGET / STAGE > 16 ? 16 : (RING_TARGET / STAGE < 2 ? 2 : RING_TARGET / STAGE);
   static constexpr int PIPE = NS * STAGE;
   // control block: full[NS], empty[NS], tinfo_full[2], acc_full[2], acc_empty[2],
@@ -53,11 +85,14 @@ struct Cfg {
   static constexpr int OFF_TMEM = OFF_AEMPTY + 16;
   static constexpr int OFF_ABORT = OFF_TMEM + 4;
   static constexpr int OFF_STEPS = OFF_ABORT + 4;   // int[2]
-  static constexpr int OFF_MASK = OFF_STEPS + 8;    // uint32
-  static constexpr int CTRL = (OFF_MASK + 4 + 127) / 128 * 128;
+  static constexpr int OFF_MASK = OFF_STEPS + 8;    // uint32 scratch for the OR reduction
+  static constexpr int OFF_KMASK = OFF_MASK + 4;    // uint32[2] active offsets per buffer
+  static constexpr int CTRL = (OFF_KMASK + 8 + 127) / 128 * 128;
   static constexpr int OROW = 2 * BMT * 4;          // out rows per accumulator buffer
-  static constexpr int ROWS = KMAX * BMT * 4;       // gather rows of the tile being produced
-  static constexpr int TOTAL = 1024 + PIPE + CTRL + OROW + ROWS;
+  static constexpr int BIAS = 256 * 4;              // fp32 bias of the column tile
+  static constexpr int ROWS = 2 * KMAX * BMT * 4;   // gather rows, double-buffered
+  static constexpr int LMASK = 2 * KMAX * 2 * 4 * 4;  // [buffer][k][half][4] disabled-row bits
+  static constexpr int TOTAL = 1024 + PIPE + CTRL + OROW + BIAS + ROWS + LMASK;
   static constexpr int SWZ_MODE = KC == 64 ? 2 : (KC == 32 ? 4 : 6);
   static constexpr int SBO = 8 * KC * 2;
 };
@@ -68,7 +103,8 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
 
 template <typename T, int TN, int KC>
 __global__ void __launch_bounds__(NT, 1)
-k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__ W,
+k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ CUtensorMap tmap_w,
+           const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__ W,
            const T* __restrict__ bias, const int32_t* __restrict__ gmap, const int32_t* __restrict__ perm, int K,
            int64_t n_out, int c_out, const int32_t* __restrict__ ovf, int64_t ovf_cap,
            const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status) {
@@ -92,8 +128,11 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
   volatile int* s_abort = reinterpret_cast<volatile int*>(ctrl + C::OFF_ABORT);
   int* s_steps = reinterpret_cast<int*>(ctrl + C::OFF_STEPS);
   unsigned* s_mask = reinterpret_cast<unsigned*>(ctrl + C::OFF_MASK);
-  int32_t* s_orow = reinterpret_cast<int32_t*>(ctrl + C::CTRL);            // [2][BMT]
-  int32_t* s_rows = reinterpret_cast<int32_t*>(ctrl + C::CTRL + C::OROW);  // [K][BMT]
+  int32_t* s_orow = reinterpret_cast<int32_t*>(ctrl + C::CTRL);                        // [2][BMT]
+  float* s_bias = reinterpret_cast<float*>(ctrl + C::CTRL + C::OROW);                  // [TN]
+  int32_t* s_rows = reinterpret_cast<int32_t*>(ctrl + C::CTRL + C::OROW + C::BIAS);    // [2][K][BMT]
+  uint32_t* s_lmask = reinterpret_cast<uint32_t*>(ctrl + C::CTRL + C::OROW + C::BIAS + C::ROWS);
+  unsigned* s_kmask = reinterpret_cast<unsigned*>(ctrl + C::OFF_KMASK);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -106,7 +145,7 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
 
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
-      tc::mbar_init(bar_full + 8 * s, NPROD);
+      tc::mbar_init(bar_full + 8 * s, NPROD / 32);  // one arrive.expect_tx per producer warp
       tc::mbar_init(bar_empty + 8 * s, 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -133,53 +172,81 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
     // Control flow is collective across the 128 producers (named barriers):
     // a failed wait clears `alive`, after which the thread skips all work but
     // still reaches every barrier.
+    //
+    // Thread p owns tile rows p and p+128.  The gather entries of the NEXT
+    // tile are copied with 4-byte cp.async into the other half of the
+    // double-buffered rows table while this tile's steps are produced, so no
+    // dependent global round trip separates two tiles.
     int64_t gstep = 0;  // steps produced so far (ring position)
     int it = 0;
     bool alive = true;
-    for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
-      const int b = it % NACC;
-      const int use = it / NACC;
+    auto out_rows = [&](int64_t t, int (&o)[2]) {
       const int64_t row_tile = t / n_col_tiles;
-      const int n0 = static_cast<int>(t - row_tile * n_col_tiles) * TN;
-      // out rows of buffer b are free once the epilogue released tile it-NACC
-      if (alive && use > 0) alive = tc::mbar_wait(bar_aempty + 8 * b, (use - 1) & 1, deadline, s_abort, status);
-      // ---- stage this thread's two rows: out row ids + gather entries ----
-      int o2[2];
-      unsigned mask = 0;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int64_t tr = row_tile * BMT + tid + h * HALF;
-        o2[h] = (alive && tr < n_out) ? (perm != nullptr ? __ldg(&perm[tr]) : static_cast<int>(tr)) : -1;
-        if (alive) s_orow[b * BMT + tid + h * HALF] = o2[h];
+        o[h] = (t < n_tiles && tr < n_out) ? (perm != nullptr ? __ldg(&perm[tr]) : static_cast<int>(tr)) : -1;
       }
-      for (int k0 = 0; k0 < K; k0 += 8) {
-        int jj[8][2];
+    };
+    auto prefetch_rows = [&](const int (&o)[2], int rb) {
+      int32_t* dst = s_rows + rb * (K * BMT);
+      for (int k = 0; k < K; ++k) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int k = k0 + q;
-            int j = -1;
-            if (k < K && o2[h] >= 0)
-              j = gmap != nullptr ? __ldg(&gmap[static_cast<int64_t>(k) * n_out + o2[h]]) : o2[h];
-            jj[q][h] = j;
-          }
+        for (int h = 0; h < 2; ++h) {
+          int32_t* d = dst + k * BMT + tid + h * HALF;
+          if (o[h] >= 0 && gmap != nullptr)
+            cp_async4(d, gmap + static_cast<int64_t>(k) * n_out + o[h]);
+          else
+            *d = o[h];  // identity map (K == 1), or -1 past the last row
         }
+      }
+      mma::cp_commit();
+    };
+    int o_cur[2], o_nxt[2];
+    out_rows(blockIdx.x, o_cur);
+    prefetch_rows(o_cur, 0);
+    for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+      const int b = it % NACC;
+      const int use = it / NACC;
+      const int rb = it & 1;
+      const int64_t row_tile = t / n_col_tiles;
+      const int n0 = static_cast<int>(t - row_tile * n_col_tiles) * TN;
+      // the other rows buffer held tile it-1, whose entries this thread has read
+      out_rows(t + gridDim.x, o_nxt);
+      prefetch_rows(o_nxt, rb ^ 1);
+      tc::cp_wait_n<1>();  // this tile's entries (committed one tile earlier) have landed
+      // buffer b (out rows, row masks, step count) is free once the epilogue
+      // released its previous tile; the epilogue's first arrival marks the
+      // freshly zeroed accumulator
+      if (alive) alive = tc::mbar_wait(bar_aempty + 8 * b, use & 1, deadline, s_abort, status);
+      int32_t* rows = s_rows + rb * (K * BMT);
+      uint32_t* lm = s_lmask + b * (KMAX * 8);
+      unsigned mask = 0;
+      for (int k = 0; k < K; ++k) {
+        bool invalid[2];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int k = k0 + q;
-          if (k >= K) break;
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            int j = jj[q][h];
-            if (j >= n_in) {
-              raise_status(status, TSC_STATUS_KEY_RANGE);
-              j = -1;
-            }
-            s_rows[k * BMT + tid + h * HALF] = j;
-            if (j >= 0) mask |= 1u << k;
+        for (int h = 0; h < 2; ++h) {
+          int32_t* p = rows + k * BMT + tid + h * HALF;
+          const int j = *p;
+          if (j >= n_in) {
+            raise_status(status, TSC_STATUS_KEY_RANGE);
+            *p = -1;
+          } else if (j >= 0) {
+            mask |= 1u << k;
           }
+          invalid[h] = !(j >= 0 && j < n_in);
         }
+        // rows without a pair are gathered from row 0 and disabled in the MMA
+        const unsigned d0 = __ballot_sync(kFullMask, invalid[0]);
+        const unsigned d1 = __ballot_sync(kFullMask, invalid[1]);
+        if (alive && lane == 0) {
+          lm[k * 8 + warp] = d0;
+          lm[k * 8 + 4 + warp] = d1;
+        }
+      }
+      if (alive) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) s_orow[b * BMT + tid + h * HALF] = o_cur[h];
       }
       // ---- tile's active offsets: OR over the 128 producers -------------------
       mask = __reduce_or_sync(kFullMask, mask);
@@ -190,7 +257,10 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
       const unsigned kmask = *s_mask;
       const int steps = alive ? __popc(kmask) * n_chunks : 0;
       if (alive) {
-        if (tid == 0) s_steps[b] = steps;
+        if (tid == 0) {
+          s_steps[b] = steps;
+          s_kmask[b] = kmask;
+        }
         tc::mbar_arrive(bar_tinfo + 8 * b);
       }
       // ---- steps -----------------------------------------------------------------
@@ -210,33 +280,30 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
           break;
         }
         const int c0 = chunk * KC;
-        unsigned char* sa = ring + stage * C::STAGE;
-        unsigned char* sb = sa + C::A_BYTES;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int r = tid + h * HALF;
-          const int j = s_rows[k * BMT + r];
-          unsigned char* drow = sa + r * (KC * 2);
-          const T* srow = F + static_cast<int64_t>(j < 0 ? 0 : j) * c_in;
-#pragma unroll
-          for (int q = 0; q < UPR; ++q) {
-            const int c = c0 + q * 8;
-            const bool valid = j >= 0 && c < c_in;
-            mma::cp_async<16>(drow + (mma::swz<KC>(r, q) << 4), valid ? srow + c : F, valid);
-          }
+        const uint32_t sa = ring_u32 + stage * C::STAGE;
+        const uint32_t sb = sa + C::A_BYTES;
+        const uint32_t full = bar_full + 8 * stage;
+        // warp w gathers tile rows [64w, 64w+64): lanes 0-15 one 4-row TMA
+        // gather each; warp 0 also loads the weight slice.  Row entries of
+        // other producers are visible after the mask barriers.
+        if (lane == 0) mbar_arrive_expect_tx(full, 64 * KC * 2 + (warp == 0 ? C::B_BYTES : 0));
+        __syncwarp();
+        if (lane < 16) {
+          const int r = warp * 64 + lane * 4;
+          const int32_t* e = rows + k * BMT + r;
+          // rows without a pair read row 0 (always present); their MMA lanes are disabled
+          const int y0 = e[0] >= 0 ? e[0] : 0;
+          const int y1 = e[1] >= 0 ? e[1] : 0;
+          const int y2 = e[2] >= 0 ? e[2] : 0;
+          const int y3 = e[3] >= 0 ? e[3] : 0;
+          tma_gather4(sa + r * (KC * 2), &tmap_f, c0, y0, y1, y2, y3, full);
+        } else if (warp == 0 && lane == 16) {
+          tma_load_3d(sb, &tmap_w, c0, k, n0, full);
         }
-        for (int u = tid; u < TN * UPR; u += NPROD) {
-          const int nn = u / UPR;
-          const int q = u - nn * UPR;
-          const int c = c0 + q * 8;
-          const int n = n0 + nn;
-          const bool valid = n < c_out && c < c_in;
-          mma::cp_async<16>(sb + nn * (KC * 2) + (mma::swz<KC>(nn, q) << 4),
-                            valid ? W + (static_cast<int64_t>(n) * K + k) * c_in + c : W, valid);
-        }
-        tc::cp_arrive_noinc(bar_full + 8 * stage);
       }
       if (*s_abort) alive = false;
+      o_cur[0] = o_nxt[0];
+      o_cur[1] = o_nxt[1];
       // s_mask is reset at the start of the next tile: every producer must
       // have read it first
       named_bar_sync(1, NPROD);
@@ -253,11 +320,19 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
         const int use = it / NACC;
         if (!tc::mbar_wait(bar_tinfo + 8 * b, use & 1, deadline, s_abort, status)) break;
         const int steps = s_steps[b];
-        if (use > 0 && !tc::mbar_wait(bar_aempty + 8 * b, (use - 1) & 1, deadline, s_abort, status)) break;
+        unsigned rem = s_kmask[b];
+        // accumulator buffer b is zeroed and drained (epilogue arrival #use)
+        if (!tc::mbar_wait(bar_aempty + 8 * b, use & 1, deadline, s_abort, status)) break;
         tc::tc_fence_after();
         const uint32_t acc0 = tmem + static_cast<uint32_t>(b * 2 * TN);
+        const uint32_t* lm = s_lmask + b * (KMAX * 8);
         bool ok = true;
+        int k = 0;
         for (int s = 0; s < steps; ++s, ++gstep) {
+          if (s % n_chunks == 0) {
+            k = __ffs(rem) - 1;
+            rem &= rem - 1;
+          }
           const int stage = static_cast<int>(gstep % NS);
           if (!tc::mbar_wait(bar_full + 8 * stage, static_cast<uint32_t>((gstep / NS) & 1), deadline, s_abort,
                              status)) {
@@ -267,15 +342,16 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
           tc::tc_fence_after();
           const uint32_t a_addr = ring_u32 + stage * C::STAGE;
           const uint32_t b_addr = a_addr + C::A_BYTES;
+          const uint32_t* mk = lm + k * 8;
 #pragma unroll
           for (int kk = 0; kk < KC / 16; ++kk) {
             const unsigned long long bd = tc::smem_desc<C::SWZ_MODE, C::SBO>(b_addr + kk * 32);
-            const uint32_t acc = (s > 0 || kk > 0) ? 1u : 0u;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              tc::umma_f16(acc0 + h * TN,
-                           tc::smem_desc<C::SWZ_MODE, C::SBO>(a_addr + h * (HALF * KC * 2) + kk * 32), bd,
-                           idesc, acc);
+              // the accumulator starts at zero; rows without a pair at offset k are disabled
+              tc::umma_f16_masked(acc0 + h * TN,
+                                  tc::smem_desc<C::SWZ_MODE, C::SBO>(a_addr + h * (HALF * KC * 2) + kk * 32), bd,
+                                  idesc, 1u, mk[h * 4 + 0], mk[h * 4 + 1], mk[h * 4 + 2], mk[h * 4 + 3]);
             }
           }
           tc::umma_commit(bar_empty + 8 * stage);
@@ -294,6 +370,27 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
       n_ovf = static_cast<int64_t>(__ldg(&meta[TSC_META_N_OVERFLOW]));
       if (n_ovf > ovf_cap) n_ovf = ovf_cap;
     }
+    // one column tile: the bias is the same for every tile -> shared memory
+    const bool bias_smem = n_col_tiles == 1;
+    if (bias_smem) {
+      for (int i = tid - (NPROD + 32); i < TN; i += NEPI)
+        s_bias[i] = (bias != nullptr && i < c_out) ? to_f32(__ldg(&bias[i])) : 0.f;
+      named_bar_sync(2, NEPI);
+    }
+    // zero both accumulator buffers (MMAs always accumulate; rows without a
+    // pair are masked off) and hand them to the MMA issuer: arrival #0
+    for (int b = 0; b < NACC; ++b) {
+      __syncwarp();
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h)
+#pragma unroll 1
+        for (int c0 = 0; c0 < TN; c0 += 32)
+          tc::tmem_st32_zero(tmem + (static_cast<uint32_t>(q * 32) << 16) +
+                             static_cast<uint32_t>(b * 2 * TN + h * TN + c0));
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      tc::mbar_arrive(bar_aempty + 8 * b);
+    }
     int it = 0;
     for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
       const int b = it % NACC;
@@ -304,7 +401,6 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
       const bool ok2 = ok1 && tc::mbar_wait(bar_afull + 8 * b, use & 1, deadline, s_abort, status);
       if (!__all_sync(kFullMask, ok2)) break;
       tc::tc_fence_after();
-      const int steps = s_steps[b];
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         const int o = s_orow[b * BMT + h * HALF + lrow];
@@ -312,13 +408,10 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
         for (int c0 = 0; c0 < TN; c0 += 32) {
           float v[32];
           __syncwarp();
-          if (steps > 0) {
-            tc::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * 2 * TN + h * TN + c0),
-                          v);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
-          }
+          const uint32_t taddr =
+              tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * 2 * TN + h * TN + c0);
+          tc::tmem_ld32(taddr, v);
+          tc::tmem_st32_zero(taddr);  // ready for the buffer's next tile
           if (o < 0 || n0 + c0 >= c_out) continue;
           for (int64_t e = 0; e < n_ovf; ++e) {
             if (__ldg(&ovf[3 * e + 1]) != o) continue;
@@ -347,7 +440,10 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               float x = v[qq * 8 + i];
-              if (bias != nullptr) x += to_f32(__ldg(&bias[n + i]));
+              if (bias_smem)
+                x += s_bias[n + i];
+              else if (bias != nullptr)
+                x += to_f32(__ldg(&bias[n + i]));
               if (relu) x = fmaxf(x, 0.f);
               pk.hv[i] = from_f32<T>(x);
             }
@@ -355,6 +451,8 @@ k_conv_tcp(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
           }
         }
       }
+      __syncwarp();
+      tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(bar_aempty + 8 * b);
     }
