@@ -143,3 +143,16 @@ def test_tc_many_tiles_per_cta(cuda, cin, cout):
     from trispconv_b200 import _lib
 
     _lib.check_device_status(cuda)
+
+
+@pytest.mark.parametrize("cin,cout", [(32, 32), (16, 16), (32, 128), (16, 256), (64, 32)])
+def test_tc_remaining_tile_shapes(cuda, tc_variant, cin, cout):
+    """The (KC, TN) tile configurations not covered above."""
+    rng = np.random.default_rng(cin * 7 + cout)
+    shape = (30, 30, 30)
+    n = 9000
+    idx = torch.from_numpy(_cloud(rng, shape, n)).to(cuda)
+    f = torch.from_numpy(rng.standard_normal((n, cin)).astype(np.float32)).to(cuda).half()
+    m = spconv.SubMConv3d(cin, cout, 3).to(cuda).half()
+    a, b = _run_both(m, lambda: spconv.SparseConvTensor(f, idx, shape, 1))
+    _assert_same(a, b, torch.float16, f"{cin}->{cout}")

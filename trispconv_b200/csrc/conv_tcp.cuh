@@ -86,13 +86,11 @@ struct Cfg {
   static constexpr int OFF_ABORT = OFF_TMEM + 4;
   static constexpr int OFF_STEPS = OFF_ABORT + 4;   // int[2]
   static constexpr int OFF_MASK = OFF_STEPS + 8;    // uint32 scratch for the OR reduction
-  static constexpr int OFF_KMASK = OFF_MASK + 4;    // uint32[2] active offsets per buffer
-  static constexpr int CTRL = (OFF_KMASK + 8 + 127) / 128 * 128;
+  static constexpr int CTRL = (OFF_MASK + 4 + 127) / 128 * 128;
   static constexpr int OROW = 2 * BMT * 4;          // out rows per accumulator buffer
   static constexpr int BIAS = 256 * 4;              // fp32 bias of the column tile
   static constexpr int ROWS = 2 * KMAX * BMT * 4;   // gather rows, double-buffered
-  static constexpr int LMASK = 2 * KMAX * 2 * 4 * 4;  // [buffer][k][half][4] disabled-row bits
-  static constexpr int TOTAL = 1024 + PIPE + CTRL + OROW + BIAS + ROWS + LMASK;
+  static constexpr int TOTAL = 1024 + PIPE + CTRL + OROW + BIAS + ROWS;
   static constexpr int SWZ_MODE = KC == 64 ? 2 : (KC == 32 ? 4 : 6);
   static constexpr int SBO = 8 * KC * 2;
 };
@@ -131,8 +129,6 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
   int32_t* s_orow = reinterpret_cast<int32_t*>(ctrl + C::CTRL);                        // [2][BMT]
   float* s_bias = reinterpret_cast<float*>(ctrl + C::CTRL + C::OROW);                  // [TN]
   int32_t* s_rows = reinterpret_cast<int32_t*>(ctrl + C::CTRL + C::OROW + C::BIAS);    // [2][K][BMT]
-  uint32_t* s_lmask = reinterpret_cast<uint32_t*>(ctrl + C::CTRL + C::OROW + C::BIAS + C::ROWS);
-  unsigned* s_kmask = reinterpret_cast<unsigned*>(ctrl + C::OFF_KMASK);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -215,15 +211,13 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
       out_rows(t + gridDim.x, o_nxt);
       prefetch_rows(o_nxt, rb ^ 1);
       tc::cp_wait_n<1>();  // this tile's entries (committed one tile earlier) have landed
-      // buffer b (out rows, row masks, step count) is free once the epilogue
+      // buffer b (out rows, step count, offsets) is free once the epilogue
       // released its previous tile; the epilogue's first arrival marks the
       // freshly zeroed accumulator
       if (alive) alive = tc::mbar_wait(bar_aempty + 8 * b, use & 1, deadline, s_abort, status);
       int32_t* rows = s_rows + rb * (K * BMT);
-      uint32_t* lm = s_lmask + b * (KMAX * 8);
       unsigned mask = 0;
       for (int k = 0; k < K; ++k) {
-        bool invalid[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           int32_t* p = rows + k * BMT + tid + h * HALF;
@@ -234,14 +228,6 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
           } else if (j >= 0) {
             mask |= 1u << k;
           }
-          invalid[h] = !(j >= 0 && j < n_in);
-        }
-        // rows without a pair are gathered from row 0 and disabled in the MMA
-        const unsigned d0 = __ballot_sync(kFullMask, invalid[0]);
-        const unsigned d1 = __ballot_sync(kFullMask, invalid[1]);
-        if (alive && lane == 0) {
-          lm[k * 8 + warp] = d0;
-          lm[k * 8 + 4 + warp] = d1;
         }
       }
       if (alive) {
@@ -257,10 +243,7 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
       const unsigned kmask = *s_mask;
       const int steps = alive ? __popc(kmask) * n_chunks : 0;
       if (alive) {
-        if (tid == 0) {
-          s_steps[b] = steps;
-          s_kmask[b] = kmask;
-        }
+        if (tid == 0) s_steps[b] = steps;
         tc::mbar_arrive(bar_tinfo + 8 * b);
       }
       // ---- steps -----------------------------------------------------------------
@@ -291,11 +274,13 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
         if (lane < 16) {
           const int r = warp * 64 + lane * 4;
           const int32_t* e = rows + k * BMT + r;
-          // rows without a pair read row 0 (always present); their MMA lanes are disabled
-          const int y0 = e[0] >= 0 ? e[0] : 0;
-          const int y1 = e[1] >= 0 ? e[1] : 0;
-          const int y2 = e[2] >= 0 ? e[2] : 0;
-          const int y3 = e[3] >= 0 ? e[3] : 0;
+          // rows without a pair use the out-of-range row index n_in: the TMA
+          // unit fills them with zeros and reads no memory for them
+          const int oob = static_cast<int>(n_in);
+          const int y0 = e[0] >= 0 ? e[0] : oob;
+          const int y1 = e[1] >= 0 ? e[1] : oob;
+          const int y2 = e[2] >= 0 ? e[2] : oob;
+          const int y3 = e[3] >= 0 ? e[3] : oob;
           tma_gather4(sa + r * (KC * 2), &tmap_f, c0, y0, y1, y2, y3, full);
         } else if (warp == 0 && lane == 16) {
           tma_load_3d(sb, &tmap_w, c0, k, n0, full);
@@ -320,19 +305,12 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
         const int use = it / NACC;
         if (!tc::mbar_wait(bar_tinfo + 8 * b, use & 1, deadline, s_abort, status)) break;
         const int steps = s_steps[b];
-        unsigned rem = s_kmask[b];
         // accumulator buffer b is zeroed and drained (epilogue arrival #use)
         if (!tc::mbar_wait(bar_aempty + 8 * b, use & 1, deadline, s_abort, status)) break;
         tc::tc_fence_after();
         const uint32_t acc0 = tmem + static_cast<uint32_t>(b * 2 * TN);
-        const uint32_t* lm = s_lmask + b * (KMAX * 8);
         bool ok = true;
-        int k = 0;
         for (int s = 0; s < steps; ++s, ++gstep) {
-          if (s % n_chunks == 0) {
-            k = __ffs(rem) - 1;
-            rem &= rem - 1;
-          }
           const int stage = static_cast<int>(gstep % NS);
           if (!tc::mbar_wait(bar_full + 8 * stage, static_cast<uint32_t>((gstep / NS) & 1), deadline, s_abort,
                              status)) {
@@ -342,16 +320,15 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
           tc::tc_fence_after();
           const uint32_t a_addr = ring_u32 + stage * C::STAGE;
           const uint32_t b_addr = a_addr + C::A_BYTES;
-          const uint32_t* mk = lm + k * 8;
 #pragma unroll
           for (int kk = 0; kk < KC / 16; ++kk) {
             const unsigned long long bd = tc::smem_desc<C::SWZ_MODE, C::SBO>(b_addr + kk * 32);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              // the accumulator starts at zero; rows without a pair at offset k are disabled
-              tc::umma_f16_masked(acc0 + h * TN,
-                                  tc::smem_desc<C::SWZ_MODE, C::SBO>(a_addr + h * (HALF * KC * 2) + kk * 32), bd,
-                                  idesc, 1u, mk[h * 4 + 0], mk[h * 4 + 1], mk[h * 4 + 2], mk[h * 4 + 3]);
+              // the accumulator starts at zero (epilogue-cleared), so every MMA accumulates
+              tc::umma_f16(acc0 + h * TN,
+                           tc::smem_desc<C::SWZ_MODE, C::SBO>(a_addr + h * (HALF * KC * 2) + kk * 32), bd, idesc,
+                           1u);
             }
           }
           tc::umma_commit(bar_empty + 8 * stage);
