@@ -11,7 +11,8 @@
  * Conventions
  *   - Every pointer argument named *_dev / device buffer is CUDA device memory
  *     allocated by the caller (the Python host uses torch's caching
- *     allocator).  The library holds no device memory of its own.
+ *     allocator).  The library holds no device memory of its own, except
+ *     the fixed table behind tsc_subm_kmap_noalloc.
  *   - `stream` is a cudaStream_t passed as void*.  All work is enqueued on it;
  *     no entry point synchronises the stream.
  *   - Host-side problems (bad arguments, misaligned pointers, launch failures)
@@ -224,6 +225,25 @@ TSC_API int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, 
 TSC_API int tsc_to_dense(const void* features, int32_t dtype, const int32_t* indices, int64_t n, int32_t c,
                  int32_t batch, const int32_t* shape3, int32_t channels_first,
                  void* out, int64_t* status, void* stream);
+
+/* ---- allocation-free submanifold kernel map ------------------------------
+ * No counterpart in the reference: an addition for callers that cannot
+ * allocate device memory when they build a map (a host that owns a fixed
+ * memory budget or pool, code that must not let cudaMalloc/cudaFree
+ * synchronise the device, bindings without a device allocator).  Same result
+ * as tsc_subm_kmap, but its hash table lives in a fixed 16 MiB device array
+ * inside this library (held on every GPU that loads the library until the
+ * process exits) instead of a caller workspace; it calls no allocator.
+ *   - n must not exceed tsc_subm_kmap_noalloc_max_voxels() (2^20); larger
+ *     inputs fail with TSC_ERR_WORKSPACE and a message naming the limit.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - All calls on a device share the one array: calls whose work overlaps
+ *     on the GPU (different streams, or threads) race and give wrong maps;
+ *     serialise them.  Each call clears the part of the table it uses. */
+TSC_API int64_t tsc_subm_kmap_noalloc_max_voxels(void);
+TSC_API int tsc_subm_kmap_noalloc(const int32_t* indices, int64_t n, const tsc_geometry* geo,
+                          int32_t* gather_map, int64_t* meta, int64_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -12,6 +12,7 @@
 // gives every output cell its rank in sorted key order.  All maps are k-major
 // int32 arrays so that per-offset reads and writes are coalesced.
 #include <cstdint>
+#include <mutex>
 
 #include "tsc_common.cuh"
 
@@ -943,6 +944,101 @@ int tsc_gather_from_pairs(const int64_t* pairs_in, const int64_t* pairs_out, con
         reinterpret_cast<unsigned long long*>(meta), status);
     TSC_LAUNCH_CHECK("k_pairs_to_gather");
   }
+  return TSC_OK;
+}
+
+}  // extern "C"
+
+// ---- allocation-free submanifold kernel map ---------------------------------
+// Some callers cannot allocate device memory at the moment they build a map:
+// code running under a caller-owned memory pool or budget that forbids
+// cudaMalloc, host code that must not synchronise the device (cudaMalloc and
+// cudaFree can), and language bindings that have no allocator of their own.
+// tsc_subm_kmap_noalloc serves them with a hash table that lives in a fixed
+// file-scope device array instead of a caller-provided workspace.
+
+namespace tsc {
+namespace {
+
+constexpr int kNoAllocLog2Cap = 21;  // 2^21 hash entries of 8 bytes = 16 MiB per device
+constexpr int64_t kNoAllocMaxVoxels = int64_t{1} << (kNoAllocLog2Cap - 1);
+constexpr int kNoAllocMaxDevices = 64;
+
+// Held by every GPU that loads this library until the process exits.  In host
+// code this name denotes a host-side stand-in, not a device address: the
+// device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned long long g_subm_scratch[size_t{1} << kNoAllocLog2Cap];
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kNoAllocMaxDevices] = {};
+
+// Device address of g_subm_scratch on the current device, looked up once per
+// device (the first call on each device does it).
+int scratch_address(void** out) {
+  int dev = 0;
+  TSC_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices) {
+    set_error("device ordinal %d exceeds the %d devices the allocation-free path supports", dev,
+              kNoAllocMaxDevices);
+    return TSC_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    TSC_CUDA(cudaGetSymbolAddress(&p, g_subm_scratch));
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return TSC_OK;
+}
+
+}  // namespace
+}  // namespace tsc
+
+extern "C" {
+
+int64_t tsc_subm_kmap_noalloc_max_voxels(void) { return tsc::kNoAllocMaxVoxels; }
+
+int tsc_subm_kmap_noalloc(const int32_t* indices, int64_t n, const tsc_geometry* geo, int32_t* gather_map,
+                          int64_t* meta, int64_t* status, void* stream_) {
+  using namespace tsc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int rc = check_geometry(geo, false);
+  if (rc != TSC_OK) return rc;
+  TSC_CHECK_ARG(n >= 0, "number of voxels %lld is negative", (long long)n);
+  if (n > kNoAllocMaxVoxels) {
+    set_error("tsc_subm_kmap_noalloc takes at most %lld voxels (fixed 16 MiB device table), got %lld; "
+              "use tsc_subm_kmap with a caller-provided workspace",
+              (long long)kNoAllocMaxVoxels, (long long)n);
+    return TSC_ERR_WORKSPACE;
+  }
+  TSC_CHECK_ARG(meta != nullptr && status != nullptr, "meta/status must not be NULL");
+  const uint64_t cells = cells_of(geo->batch, geo->in_shape);
+  if (cells > kMaxCells) {
+    set_error("grid batch*D*H*W = %llu exceeds the packed-key limit 2^32-2", (unsigned long long)cells);
+    return TSC_ERR_GRID_TOO_LARGE;
+  }
+  void* scratch = nullptr;
+  rc = scratch_address(&scratch);
+  if (rc != TSC_OK) return rc;
+  const int K = geo->ksize[0] * geo->ksize[1] * geo->ksize[2];
+  TSC_CUDA(cudaMemsetAsync(meta, 0, sizeof(int64_t) * (TSC_META_COUNTS + K), stream));
+  if (n == 0) return TSC_OK;
+  TSC_CHECK_ARG(indices != nullptr && aligned(indices, 16), "indices must be 16-byte aligned");
+  TSC_CHECK_ARG(gather_map != nullptr && aligned(gather_map, 4), "gather_map must not be NULL");
+  // same table capacity as tsc_subm_kmap; the part in use is reset on every
+  // call because the array keeps the previous call's entries
+  const int log2cap = subm_log2cap(n);
+  auto* table = static_cast<unsigned long long*>(scratch);
+  TSC_CUDA(cudaMemsetAsync(table, 0xFF, static_cast<size_t>(8) << log2cap, stream));
+  const GeoDev g = to_dev(*geo);
+  const int4* idx = reinterpret_cast<const int4*>(indices);
+  const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
+  k_hash_build<<<grid, kThreads, 0, stream>>>(idx, n, g.B, g.D, g.H, g.W, table, log2cap, status);
+  TSC_LAUNCH_CHECK("k_hash_build");
+  k_subm_query<<<dim3(grid, K), kThreads, 0, stream>>>(idx, n, g, table, log2cap, gather_map,
+                                                       reinterpret_cast<unsigned long long*>(meta));
+  TSC_LAUNCH_CHECK("k_subm_query");
   return TSC_OK;
 }
 
