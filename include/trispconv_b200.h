@@ -57,6 +57,7 @@ extern "C" {
 #define TSC_STATUS_HASH_FULL      0x2  /* open-addressing table ran out of probes */
 #define TSC_STATUS_OVERFLOW_FULL  0x4  /* duplicate-pair overflow list ran out of room */
 #define TSC_STATUS_WAIT_TIMEOUT   0x8  /* a kernel gave up waiting on one of its own barriers */
+#define TSC_STATUS_INTERNAL       0x10 /* a kernel found an out-of-range index in its own shared state and skipped it */
 
 /* Feature / weight element types. */
 #define TSC_F32  0
@@ -210,7 +211,10 @@ TSC_API int tsc_gather_from_pairs(const int64_t* pairs_in, const int64_t* pairs_
  * is a permutation of [0, n_out) giving the order in which output rows are
  * grouped into tiles; results do not depend on it.  16-bit dtypes with KRSC
  * weights, C_in % 8 == 0 (or C_in % 4 == 0 and C_in <= 16), C_out % 8 == 0
- * and K <= 64 run on the tensor cores; everything else on the CUDA cores. */
+ * and K <= 64 run on the tensor cores (mma.sync); with TSC_CONV_USE_TC,
+ * layers with C_in % 32 == 0, C_out % 32 == 0 and K <= 27 run on the
+ * persistent tcgen05/TMEM kernel instead.  Everything else runs on the CUDA
+ * cores. */
 TSC_API int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t c_in,
                      const void* weight, int32_t weight_layout, const void* bias,
                      const int32_t* gather_map, const int32_t* row_order,

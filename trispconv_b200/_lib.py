@@ -28,6 +28,7 @@ STATUS_KEY_RANGE = 0x1
 STATUS_HASH_FULL = 0x2
 STATUS_OVERFLOW_FULL = 0x4
 STATUS_WAIT_TIMEOUT = 0x8
+STATUS_INTERNAL = 0x10
 
 META_N_OUT = 0
 META_N_PART = 1
@@ -189,6 +190,8 @@ def decode_status(bits: int) -> str:
         names.append("duplicate-pair overflow list is full")
     if bits & STATUS_WAIT_TIMEOUT:
         names.append("a kernel timed out waiting on its own pipeline barrier")
+    if bits & STATUS_INTERNAL:
+        names.append("a kernel found an out-of-range index in its own shared state (internal error)")
     return "; ".join(names) or f"status 0x{bits:x}"
 
 

@@ -255,10 +255,13 @@ int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t 
   const ConvArgs a{features, n_in, c_in, weight, bias, gather_map, row_order, k_vol, n_out, c_out,
                    overflow, overflow_cap, meta, out, flags, status, stream};
   const bool f16 = dtype == TSC_F16;
-  if (!force_simt && (flags & TSC_CONV_USE_TC) != 0 && tc_eligible(dtype, w_krsc, c_in, c_out, k_vol)) {
-    if (n_in > 0 && k_vol <= kPersistentKMax && (flags & TSC_CONV_TC_SIMPLE) == 0)
+  if (!force_simt && (flags & TSC_CONV_USE_TC) != 0) {
+    // the one-tile-per-CTA kernel only on request (testing); otherwise the
+    // persistent kernel where its tile shapes apply, else mma.sync below
+    if ((flags & TSC_CONV_TC_SIMPLE) != 0 && tc_eligible(dtype, w_krsc, c_in, c_out, k_vol))
+      return f16 ? launch_tc_f16(a) : launch_tc_bf16(a);
+    if (n_in > 0 && tcp_eligible(dtype, w_krsc, c_in, c_out, k_vol) && (flags & TSC_CONV_TC_SIMPLE) == 0)
       return f16 ? launch_tcp_f16(a) : launch_tcp_bf16(a);
-    return f16 ? launch_tc_f16(a) : launch_tc_bf16(a);
   }
   if (!force_simt && mma_eligible(dtype, w_krsc, c_in, c_out, k_vol))
     return f16 ? launch_mma_f16(a) : launch_mma_bf16(a);

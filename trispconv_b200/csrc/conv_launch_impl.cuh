@@ -114,8 +114,8 @@ constexpr CUtensorMapSwizzle tma_swizzle() {
 
 // Features [n_in][c_in] as a 2-D tensor {c_in, n_in}, box {KC, 1} (gather4),
 // and KRSC weights [c_out][K][c_in] as a 3-D tensor {c_in, K, c_out}, box
-// {KC, 1, TN}; both swizzled like the UMMA K-major operand tiles, zero fill
-// outside the tensor.
+// {KC, 1, TN}; both swizzled like the UMMA K-major operand tiles.  The
+// kernel issues only boxes and gather rows that lie inside the tensors.
 template <typename T, int TN, int KC>
 int encode_maps(const T* f, int64_t n_in, int c_in, const T* w, int K, int c_out, CUtensorMap* mf, CUtensorMap* mw) {
   EncodeTiledFn enc;
@@ -178,13 +178,11 @@ template <typename T, int TN>
 int launch_tcp_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                   const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
                   const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
-  if (c_in <= 16)
-    return launch_tcp_cfg<T, TN, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
+  // KC (64 or 32) divides c_in (tcp_eligible): every feature and weight box lies inside its tensor
+  if (c_in % 64 == 0)
+    return launch_tcp_cfg<T, TN, 64>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
                                      flags, status, stream);
-  if (c_in <= 32)
-    return launch_tcp_cfg<T, TN, 32>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                     flags, status, stream);
-  return launch_tcp_cfg<T, TN, 64>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
+  return launch_tcp_cfg<T, TN, 32>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
                                    flags, status, stream);
 }
 
@@ -196,17 +194,18 @@ int launch_tcp(const void* F, int64_t n_in, int c_in, const void* W, const void*
   const T* w = static_cast<const T*>(W);
   const T* b = static_cast<const T*>(bias);
   T* o = static_cast<T*>(out);
-  if (c_out <= 32)
-    return launch_tcp_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                status, stream);
-  if (c_out <= 64)
-    return launch_tcp_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                status, stream);
-  if (c_out <= 128)
+  // the largest UMMA N that divides c_out (tcp_eligible: c_out % 32 == 0)
+  if (c_out % 256 == 0)
+    return launch_tcp_tn<T, 256>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                                 status, stream);
+  if (c_out % 128 == 0)
     return launch_tcp_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
                                  status, stream);
-  return launch_tcp_tn<T, 256>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                               status, stream);
+  if (c_out % 64 == 0)
+    return launch_tcp_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                                status, stream);
+  return launch_tcp_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+                              status, stream);
 }
 
 

@@ -152,15 +152,15 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, unsigned long long a, 
       : "memory");
 }
 
-// Same, with a per-row disable mask: D rows (TMEM lanes) whose bit is set in
-// {m0..m3} (lane i -> m[i / 32] bit i % 32) are left unchanged.
+// Same, with a disable-output-lane mask: accumulator rows (TMEM lanes) whose
+// bit is set in {m0..m3} (lane i -> m[i / 32] bit i % 32) are left unchanged.
 __device__ __forceinline__ void umma_f16_masked(uint32_t tmem_d, unsigned long long a, unsigned long long b,
-                                                uint32_t idesc, uint32_t accumulate, uint32_t m0, uint32_t m1,
-                                                uint32_t m2, uint32_t m3) {
+                                                uint32_t idesc, uint32_t m0, uint32_t m1, uint32_t m2,
+                                                uint32_t m3) {
   asm volatile(
-      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p; }"
-      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3)
+      "{ .reg .pred p; setp.ne.b32 p, 1, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%4, %5, %6, %7}, p; }"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(m0), "r"(m1), "r"(m2), "r"(m3)
       : "memory");
 }
 
@@ -176,6 +176,20 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
+}
+
+// Ring tail: waits until the tcgen05.commit arrivals that released the last
+// fill of every stage have landed on empty[stage].  A commit arrives
+// asynchronously when its MMAs complete; without this wait the CTA could exit
+// first and the arrival would land in the shared memory of the next CTA that
+// the SM runs (another launch's barriers, TMEM address or row tables).
+// `steps` ring steps were produced and consumed in total.
+__device__ __forceinline__ void drain_ring(uint32_t bar_empty, int ns, int64_t steps, unsigned long long deadline,
+                                           volatile int* abort_flag, int64_t* status) {
+  for (int s = 0; s < ns && s < steps; ++s) {
+    const int64_t fills = steps / ns + (s < steps % ns ? 1 : 0);
+    if (!mbar_wait(bar_empty + 8 * s, static_cast<uint32_t>((fills - 1) & 1), deadline, abort_flag, status)) return;
+  }
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
@@ -337,6 +351,8 @@ k_conv_tc(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__
   // ---- epilogue: warps 0-3, thread r <-> TMEM lane r <-> tile row r --------
   if (warp < 4) {
     const bool ok = __all_sync(kFullMask, mbar_wait(bar_done, 0, deadline, s_abort, status));
+    // every MMA has completed: collect the ring's last empty arrivals
+    if (tid == 0 && ok && !*s_abort) drain_ring(bar_empty, NS, steps, deadline, s_abort, status);
     tc_fence_after();
     const int r = tid;
     const int o = s_orow[r];
@@ -355,6 +371,10 @@ k_conv_tc(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      if (o >= n_out) {
+        raise_status(status, TSC_STATUS_INTERNAL);
+        continue;
       }
       if (o < 0 || n0 + c0 >= c_out) continue;
       for (int64_t e = 0; e < n_ovf; ++e) {

@@ -2,24 +2,33 @@
 //
 // One CTA per SM walks a strided list of tiles.  A tile is 256 output rows
 // x TN output channels, computed as two UMMA M=128 halves that share every
-// weight stage (half the weight traffic of 128-row tiles).  Warp roles
-// (288 threads):
-//   warps 0-3  producers.  Thread p owns tile rows p and p+128: it loads their
-//              gather-map entries for all offsets (batched, one round trip),
-//              the tile's active-offset mask is OR-reduced across producers,
-//              and for every (active offset, channel chunk) step the thread
-//              cp.async-gathers its two rows into the shared-memory ring
-//              (rows without a pair zero-filled), together with its share of
-//              the weight slice W[:, k, chunk]; the copy engine arrives on
-//              full[stage] when the copies land (cp.async.mbarrier.arrive.noinc).
+// weight stage.  Warp roles (288 threads):
+//   warps 0-3  producers, TMA only.  For every (active offset k, channel
+//              chunk) step of a tile, lanes 0-15 of warp w each cover one
+//              quad of tile rows 64w+4l..+3: a quad with at least one pair is
+//              fetched with one TMA gather4 (rows without a pair inside it
+//              repeat a valid row of the quad and are masked off in the MMA);
+//              a quad without pairs is not fetched at all.  Warp 0 also loads
+//              the weight slice W[n0:n0+TN, k, chunk] with a TMA tile load.
+//              No TMA coordinate ever lies outside its tensor.
 //   warp 4     one thread issues tcgen05.mma (M=128, N=TN, K=16) for both
-//              halves into a TMEM accumulator buffer; tcgen05.commit frees the
-//              stage (empty[stage]) and, after the tile, signals acc_full[b].
-//   warps 5-8  epilogue: tcgen05.ld of the finished buffer (warp w reads TMEM
-//              lanes 32*(w%4)..+31 of both halves), overflow pairs, bias,
-//              ReLU, 16-byte stores; then acc_empty[b].
+//              halves into a TMEM accumulator, with the per-row
+//              disable-output-lane mask of the offset; halves without any
+//              pair are skipped.  tcgen05.commit frees the stage and, after
+//              the tile, signals acc_full[b].
+//   warps 5-8  epilogue and tile set-up.  Warp w owns TMEM lanes
+//              32*(w%4)..+31 of both halves (tile rows q*32+lane and
+//              128+q*32+lane, q = w%4).  For each finished tile it reads the
+//              accumulator (tcgen05.ld), clears it for reuse, adds overflow
+//              pairs and bias, applies ReLU and stores 16-byte vectors.  It
+//              then prepares the tile two ahead: output rows, validated
+//              gather entries, per-offset lane masks and active offsets, in a
+//              double-buffered "tile info" block.  Set-up thus runs under the
+//              MMAs of the current tile instead of stalling the producers.
 // Two accumulator buffers (when 4*TN <= 512 TMEM columns) let the epilogue of
-// one tile run under the MMAs of the next.  All mbarrier waits are bounded.
+// one tile run under the MMAs of the next.  All mbarrier waits are bounded;
+// no role uses a named barrier after the start, so a role that gives up
+// cannot strand the others.
 #pragma once
 
 #include <cuda.h>
@@ -31,22 +40,19 @@ namespace tcp {
 
 constexpr int BMT = 256;       // rows per tile
 constexpr int HALF = 128;      // rows per UMMA
-constexpr int NPROD = 128;     // producer threads
-constexpr int NEPI = 128;      // epilogue threads
+constexpr int NPROD = 128;     // producer threads (warps 0-3)
+constexpr int NEPI = 128;      // epilogue threads (warps 5-8)
+constexpr int EPI0 = NPROD + 32;
 constexpr int NT = NPROD + 32 + NEPI;
 constexpr int KMAX = 27;       // offsets per map (3x3x3 and smaller; 32-bit active mask)
-
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(mma::smem_u32(dst)), "l"(src) : "memory");
-}
+constexpr int SMEM_MAX = 227 * 1024;
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-// TMA gather of 4 feature rows (y0..y3; an out-of-range row index reads the
-// zero fill) x box-width channels starting at channel x, into 4 consecutive
-// swizzled shared-memory rows at dst.
+// TMA gather of 4 feature rows y0..y3 (all inside the tensor) x box-width
+// channels starting at channel x, into 4 consecutive swizzled rows at dst.
 __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* tmap, int x, int y0, int y1, int y2,
                                             int y3, uint32_t bar) {
   asm volatile(
@@ -56,8 +62,8 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* tma
       : "memory");
 }
 
-// TMA tile load of the weight slice W[n0:n0+TN, k, c0:c0+KC] (KRSC viewed as
-// a 3-D tensor {C_in, K, C_out}); out-of-range channels read the zero fill.
+// TMA tile load of the weight slice W[z:z+TN, y, x:x+KC] (KRSC viewed as a
+// 3-D tensor {C_in, K, C_out}); the launcher guarantees the box lies inside.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tmap, int x, int y, int z, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
@@ -66,38 +72,53 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* tma
       : "memory");
 }
 
+// Per-tile information block, double-buffered (tile parity).
+struct Info {
+  static constexpr int ROWS = KMAX * BMT * 4;      // int32 gather entry [k][row], -1 = no pair
+  static constexpr int OROW = BMT * 4;             // int32 output row, -1 past the end
+  static constexpr int LMASK = KMAX * 2 * 4 * 4;   // uint32 [k][half][word]: rows WITHOUT a pair
+  static constexpr int KMASK = 4 * 4;              // uint32 [epilogue warp]: active offsets, OR them
+  static constexpr int OFF_ROWS = 0;
+  static constexpr int OFF_OROW = OFF_ROWS + ROWS;
+  static constexpr int OFF_LMASK = OFF_OROW + OROW;
+  static constexpr int OFF_KMASK = OFF_LMASK + LMASK;
+  static constexpr int BYTES = (OFF_KMASK + KMASK + 127) / 128 * 128;
+};
+
 template <int TN, int KC>
 struct Cfg {
+  static_assert(TN >= 32 && (KC == 32 || KC == 64), "persistent kernel tile shape");
   static constexpr int NACC = (4 * TN <= 512) ? 2 : 1;
   static constexpr int TMEM_COLS = NACC * 2 * TN;  // 128, 256 or 512
   static constexpr int A_BYTES = BMT * KC * 2;
   static constexpr int B_BYTES = TN * KC * 2;
-  static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int RING_TARGET = 160 * 1024;
-  static constexpr int NS = RING_TARGET / STAGE > 16 ? 16 : (RING_TARGET / STAGE < 2 ? 2 : RING_TARGET / STAGE);
+  // stages start on 1024-byte boundaries (swizzle atoms are address based)
+  static constexpr int STAGE = (A_BYTES + B_BYTES + 1023) / 1024 * 1024;
+  // control block: full[NS], empty[NS], ifull[2], iempty[2], afull[2],
+  // aempty[2], tmem addr, abort
+  static constexpr int CTRL_MAX = 16 * 16 + 64 + 16;
+  static constexpr int BIAS = 256 * 4;
+  static constexpr int FIXED = 1024 /*alignment slack*/ + 2 * Info::BYTES + BIAS + (CTRL_MAX + 127) / 128 * 128;
+  static constexpr int NS_FIT = (SMEM_MAX - FIXED) / STAGE;
+  static constexpr int NS = NS_FIT > 16 ? 16 : NS_FIT;
+  static_assert(NS >= 2, "tile configuration does not fit shared memory");
   static constexpr int PIPE = NS * STAGE;
-  // control block: full[NS], empty[NS], tinfo_full[2], acc_full[2], acc_empty[2],
-  // tmem addr, abort, steps[2], active mask scratch
   static constexpr int OFF_EMPTY = 8 * NS;
-  static constexpr int OFF_TINFO = 16 * NS;
-  static constexpr int OFF_AFULL = OFF_TINFO + 16;
+  static constexpr int OFF_IFULL = 16 * NS;
+  static constexpr int OFF_IEMPTY = OFF_IFULL + 16;
+  static constexpr int OFF_AFULL = OFF_IEMPTY + 16;
   static constexpr int OFF_AEMPTY = OFF_AFULL + 16;
   static constexpr int OFF_TMEM = OFF_AEMPTY + 16;
   static constexpr int OFF_ABORT = OFF_TMEM + 4;
-  static constexpr int OFF_STEPS = OFF_ABORT + 4;   // int[2]
-  static constexpr int OFF_MASK = OFF_STEPS + 8;    // uint32 scratch for the OR reduction
-  static constexpr int CTRL = (OFF_MASK + 4 + 127) / 128 * 128;
-  static constexpr int OROW = 2 * BMT * 4;          // out rows per accumulator buffer
-  static constexpr int BIAS = 256 * 4;              // fp32 bias of the column tile
-  static constexpr int ROWS = 2 * KMAX * BMT * 4;   // gather rows, double-buffered
-  static constexpr int TOTAL = 1024 + PIPE + CTRL + OROW + BIAS + ROWS;
+  static constexpr int CTRL = (OFF_ABORT + 4 + 127) / 128 * 128;
+  static_assert(CTRL <= (CTRL_MAX + 127) / 128 * 128, "control block");
+  static constexpr int OFF_INFO = PIPE + CTRL;         // from the ring base
+  static constexpr int OFF_BIAS = OFF_INFO + 2 * Info::BYTES;
+  static constexpr int TOTAL = 1024 + OFF_BIAS + BIAS;
+  static_assert(TOTAL <= SMEM_MAX, "shared memory");
   static constexpr int SWZ_MODE = KC == 64 ? 2 : (KC == 32 ? 4 : 6);
   static constexpr int SBO = 8 * KC * 2;
 };
-
-__device__ __forceinline__ void named_bar_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 
 template <typename T, int TN, int KC>
 __global__ void __launch_bounds__(NT, 1)
@@ -109,7 +130,6 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
   using C = Cfg<TN, KC>;
   constexpr int NS = C::NS;
   constexpr int NACC = C::NACC;
-  constexpr int UPR = KC * 2 / 16;
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = mma::smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw_u32 & 1023u)) & 1023u;
@@ -119,25 +139,30 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
   const uint32_t ctrl_u32 = ring_u32 + C::PIPE;
   const uint32_t bar_full = ctrl_u32;
   const uint32_t bar_empty = ctrl_u32 + C::OFF_EMPTY;
-  const uint32_t bar_tinfo = ctrl_u32 + C::OFF_TINFO;
+  const uint32_t bar_ifull = ctrl_u32 + C::OFF_IFULL;
+  const uint32_t bar_iempty = ctrl_u32 + C::OFF_IEMPTY;
   const uint32_t bar_afull = ctrl_u32 + C::OFF_AFULL;
   const uint32_t bar_aempty = ctrl_u32 + C::OFF_AEMPTY;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(ctrl + C::OFF_TMEM);
   volatile int* s_abort = reinterpret_cast<volatile int*>(ctrl + C::OFF_ABORT);
-  int* s_steps = reinterpret_cast<int*>(ctrl + C::OFF_STEPS);
-  unsigned* s_mask = reinterpret_cast<unsigned*>(ctrl + C::OFF_MASK);
-  int32_t* s_orow = reinterpret_cast<int32_t*>(ctrl + C::CTRL);                        // [2][BMT]
-  float* s_bias = reinterpret_cast<float*>(ctrl + C::CTRL + C::OROW);                  // [TN]
-  int32_t* s_rows = reinterpret_cast<int32_t*>(ctrl + C::CTRL + C::OROW + C::BIAS);    // [2][K][BMT]
+  unsigned char* info0 = ring + C::OFF_INFO;
+  float* s_bias = reinterpret_cast<float*>(ring + C::OFF_BIAS);
+  auto rows_of = [&](int ib) { return reinterpret_cast<int32_t*>(info0 + ib * Info::BYTES + Info::OFF_ROWS); };
+  auto orow_of = [&](int ib) { return reinterpret_cast<int32_t*>(info0 + ib * Info::BYTES + Info::OFF_OROW); };
+  auto lmask_of = [&](int ib) { return reinterpret_cast<uint32_t*>(info0 + ib * Info::BYTES + Info::OFF_LMASK); };
+  auto kmask_of = [&](int ib) {
+    const uint32_t* p = reinterpret_cast<const uint32_t*>(info0 + ib * Info::BYTES + Info::OFF_KMASK);
+    return p[0] | p[1] | p[2] | p[3];
+  };
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const unsigned long long deadline = tc::globaltimer() + tc::kWaitNs;
+  const unsigned long long deadline = 0;  // waits are bounded by a cycle count
   const int64_t n_row_tiles = (n_out + BMT - 1) / BMT;
   const int n_col_tiles = (c_out + TN - 1) / TN;
   const int64_t n_tiles = n_row_tiles * n_col_tiles;
-  const int n_chunks = (c_in + KC - 1) / KC;
+  const int n_chunks = c_in / KC;  // the launcher guarantees c_in % KC == 0
 
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -145,7 +170,8 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
       tc::mbar_init(bar_empty + 8 * s, 1);
     }
     for (int b = 0; b < 2; ++b) {
-      tc::mbar_init(bar_tinfo + 8 * b, NPROD);
+      tc::mbar_init(bar_ifull + 8 * b, NEPI);
+      tc::mbar_init(bar_iempty + 8 * b, NPROD / 32 + 1);  // producer warps + MMA issuer
       tc::mbar_init(bar_afull + 8 * b, 1);
       tc::mbar_init(bar_aempty + 8 * b, NEPI);
     }
@@ -165,91 +191,21 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
 
   if (warp < 4) {
     // =============================== producers ===============================
-    // Control flow is collective across the 128 producers (named barriers):
-    // a failed wait clears `alive`, after which the thread skips all work but
-    // still reaches every barrier.
-    //
-    // Thread p owns tile rows p and p+128.  The gather entries of the NEXT
-    // tile are copied with 4-byte cp.async into the other half of the
-    // double-buffered rows table while this tile's steps are produced, so no
-    // dependent global round trip separates two tiles.
-    int64_t gstep = 0;  // steps produced so far (ring position)
+    int64_t gstep = 0;  // ring position (same sequence in every producer warp)
     int it = 0;
-    bool alive = true;
-    auto out_rows = [&](int64_t t, int (&o)[2]) {
-      const int64_t row_tile = t / n_col_tiles;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int64_t tr = row_tile * BMT + tid + h * HALF;
-        o[h] = (t < n_tiles && tr < n_out) ? (perm != nullptr ? __ldg(&perm[tr]) : static_cast<int>(tr)) : -1;
-      }
-    };
-    auto prefetch_rows = [&](const int (&o)[2], int rb) {
-      int32_t* dst = s_rows + rb * (K * BMT);
-      for (int k = 0; k < K; ++k) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          int32_t* d = dst + k * BMT + tid + h * HALF;
-          if (o[h] >= 0 && gmap != nullptr)
-            cp_async4(d, gmap + static_cast<int64_t>(k) * n_out + o[h]);
-          else
-            *d = o[h];  // identity map (K == 1), or -1 past the last row
-        }
-      }
-      mma::cp_commit();
-    };
-    int o_cur[2], o_nxt[2];
-    out_rows(blockIdx.x, o_cur);
-    prefetch_rows(o_cur, 0);
     for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
-      const int b = it % NACC;
-      const int use = it / NACC;
-      const int rb = it & 1;
+      const int ib = it & 1;
+      const bool ok = __all_sync(kFullMask, tc::mbar_wait(bar_ifull + 8 * ib, (it >> 1) & 1, deadline, s_abort,
+                                                          status));
+      if (!ok) break;
       const int64_t row_tile = t / n_col_tiles;
       const int n0 = static_cast<int>(t - row_tile * n_col_tiles) * TN;
-      // the other rows buffer held tile it-1, whose entries this thread has read
-      out_rows(t + gridDim.x, o_nxt);
-      prefetch_rows(o_nxt, rb ^ 1);
-      tc::cp_wait_n<1>();  // this tile's entries (committed one tile earlier) have landed
-      // buffer b (out rows, step count, offsets) is free once the epilogue
-      // released its previous tile; the epilogue's first arrival marks the
-      // freshly zeroed accumulator
-      if (alive) alive = tc::mbar_wait(bar_aempty + 8 * b, use & 1, deadline, s_abort, status);
-      int32_t* rows = s_rows + rb * (K * BMT);
-      unsigned mask = 0;
-      for (int k = 0; k < K; ++k) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          int32_t* p = rows + k * BMT + tid + h * HALF;
-          const int j = *p;
-          if (j >= n_in) {
-            raise_status(status, TSC_STATUS_KEY_RANGE);
-            *p = -1;
-          } else if (j >= 0) {
-            mask |= 1u << k;
-          }
-        }
-      }
-      if (alive) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) s_orow[b * BMT + tid + h * HALF] = o_cur[h];
-      }
-      // ---- tile's active offsets: OR over the 128 producers -------------------
-      mask = __reduce_or_sync(kFullMask, mask);
-      if (tid == 0) *s_mask = 0;
-      named_bar_sync(1, NPROD);
-      if (lane == 0) atomicOr(s_mask, mask);
-      named_bar_sync(1, NPROD);
-      const unsigned kmask = *s_mask;
-      const int steps = alive ? __popc(kmask) * n_chunks : 0;
-      if (alive) {
-        if (tid == 0) s_steps[b] = steps;
-        tc::mbar_arrive(bar_tinfo + 8 * b);
-      }
-      // ---- steps -----------------------------------------------------------------
-      unsigned rem = kmask;
+      const int32_t* rows = rows_of(ib);
+      unsigned rem = kmask_of(ib);
+      const int steps = __popc(rem) * n_chunks;
       int k = 0;
-      for (int s = 0; s < steps && alive; ++s, ++gstep) {
+      bool alive = true;
+      for (int s = 0; s < steps; ++s, ++gstep) {
         const int chunk = s % n_chunks;
         if (chunk == 0) {
           k = __ffs(rem) - 1;
@@ -257,43 +213,51 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
         }
         const int stage = static_cast<int>(gstep % NS);
         const int64_t fill = gstep / NS;
-        if (fill > 0 && !tc::mbar_wait(bar_empty + 8 * stage, static_cast<uint32_t>((fill - 1) & 1), deadline,
-                                       s_abort, status)) {
+        if (fill > 0 && !__all_sync(kFullMask, tc::mbar_wait(bar_empty + 8 * stage,
+                                                              static_cast<uint32_t>((fill - 1) & 1), deadline,
+                                                              s_abort, status))) {
           alive = false;
           break;
         }
-        const int c0 = chunk * KC;
         const uint32_t sa = ring_u32 + stage * C::STAGE;
-        const uint32_t sb = sa + C::A_BYTES;
         const uint32_t full = bar_full + 8 * stage;
-        // warp w gathers tile rows [64w, 64w+64): lanes 0-15 one 4-row TMA
-        // gather each; warp 0 also loads the weight slice.  Row entries of
-        // other producers are visible after the mask barriers.
-        if (lane == 0) mbar_arrive_expect_tx(full, 64 * KC * 2 + (warp == 0 ? C::B_BYTES : 0));
+        // this lane's quad of tile rows; rows without a pair repeat the
+        // quad's first valid row (masked off in the MMA)
+        const int r = warp * 64 + (lane & 15) * 4;
+        const int4 e = *reinterpret_cast<const int4*>(rows + k * BMT + r);
+        const int first = e.x >= 0 ? e.x : (e.y >= 0 ? e.y : (e.z >= 0 ? e.z : e.w));
+        // every coordinate handed to the TMA lies inside its tensor (the
+        // set-up validated the entries; a violation is reported, not issued)
+        const bool in_rows = e.x < n_in && e.y < n_in && e.z < n_in && e.w < n_in;
+        const bool in_cols = (chunk + 1) * KC <= c_in;
+        bool fetch = lane < 16 && first >= 0;
+        if (fetch && !(in_rows && in_cols)) {
+          raise_status(status, TSC_STATUS_INTERNAL);
+          fetch = false;
+        }
+        const bool wload = warp == 0 && lane == 16;
+        const bool w_ok = k < K && n0 + TN <= c_out && in_cols;
+        if (wload && !w_ok) raise_status(status, TSC_STATUS_INTERNAL);
+        const unsigned quads = __ballot_sync(kFullMask, fetch);
+        const bool w_issue = __shfl_sync(kFullMask, w_ok, 16);
+        if (lane == 0)
+          mbar_arrive_expect_tx(full, __popc(quads) * 4 * KC * 2 + (warp == 0 && w_issue ? C::B_BYTES : 0));
         __syncwarp();
-        if (lane < 16) {
-          const int r = warp * 64 + lane * 4;
-          const int32_t* e = rows + k * BMT + r;
-          // rows without a pair use the out-of-range row index n_in: the TMA
-          // unit fills them with zeros and reads no memory for them
-          const int oob = static_cast<int>(n_in);
-          const int y0 = e[0] >= 0 ? e[0] : oob;
-          const int y1 = e[1] >= 0 ? e[1] : oob;
-          const int y2 = e[2] >= 0 ? e[2] : oob;
-          const int y3 = e[3] >= 0 ? e[3] : oob;
-          tma_gather4(sa + r * (KC * 2), &tmap_f, c0, y0, y1, y2, y3, full);
-        } else if (warp == 0 && lane == 16) {
-          tma_load_3d(sb, &tmap_w, c0, k, n0, full);
+        if (fetch) {
+          tma_gather4(sa + r * (KC * 2), &tmap_f, chunk * KC, e.x >= 0 ? e.x : first, e.y >= 0 ? e.y : first,
+                      e.z >= 0 ? e.z : first, e.w >= 0 ? e.w : first, full);
+        } else if (wload && w_ok) {
+          tma_load_3d(sa + C::A_BYTES, &tmap_w, chunk * KC, k, n0, full);
         }
       }
-      if (*s_abort) alive = false;
-      o_cur[0] = o_nxt[0];
-      o_cur[1] = o_nxt[1];
-      // s_mask is reset at the start of the next tile: every producer must
-      // have read it first
-      named_bar_sync(1, NPROD);
+      if (!alive) break;
+      // this warp has read the tile's entries: release the info block
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar_iempty + 8 * ib);
     }
-    tc::cp_wait_all();
+    // the MMA issuer releases the last fill of each stage asynchronously:
+    // collect those arrivals before the CTA may exit
+    if (tid == 0 && !*s_abort) tc::drain_ring(bar_empty, NS, gstep, deadline, s_abort, status);
   } else if (warp == 4) {
     // ================================ MMA issuer ================================
     if (lane == 0) {
@@ -301,16 +265,27 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
       int64_t gstep = 0;
       int it = 0;
       for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+        const int ib = it & 1;
         const int b = it % NACC;
         const int use = it / NACC;
-        if (!tc::mbar_wait(bar_tinfo + 8 * b, use & 1, deadline, s_abort, status)) break;
-        const int steps = s_steps[b];
+        if (!tc::mbar_wait(bar_ifull + 8 * ib, (it >> 1) & 1, deadline, s_abort, status)) break;
+        unsigned rem = kmask_of(ib);
+        const int steps = __popc(rem) * n_chunks;
+        const uint32_t* lmask = lmask_of(ib);
         // accumulator buffer b is zeroed and drained (epilogue arrival #use)
         if (!tc::mbar_wait(bar_aempty + 8 * b, use & 1, deadline, s_abort, status)) break;
         tc::tc_fence_after();
         const uint32_t acc0 = tmem + static_cast<uint32_t>(b * 2 * TN);
         bool ok = true;
+        int k = 0;
+        uint4 m[2];
         for (int s = 0; s < steps; ++s, ++gstep) {
+          if (s % n_chunks == 0) {
+            k = __ffs(rem) - 1;
+            rem &= rem - 1;
+            m[0] = *reinterpret_cast<const uint4*>(lmask + (k * 2 + 0) * 4);
+            m[1] = *reinterpret_cast<const uint4*>(lmask + (k * 2 + 1) * 4);
+          }
           const int stage = static_cast<int>(gstep % NS);
           if (!tc::mbar_wait(bar_full + 8 * stage, static_cast<uint32_t>((gstep / NS) & 1), deadline, s_abort,
                              status)) {
@@ -321,24 +296,24 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
           const uint32_t a_addr = ring_u32 + stage * C::STAGE;
           const uint32_t b_addr = a_addr + C::A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < KC / 16; ++kk) {
-            const unsigned long long bd = tc::smem_desc<C::SWZ_MODE, C::SBO>(b_addr + kk * 32);
+          for (int h = 0; h < 2; ++h) {
+            if ((m[h].x & m[h].y & m[h].z & m[h].w) == kFullMask) continue;  // no pair in this half
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              // the accumulator starts at zero (epilogue-cleared), so every MMA accumulates
-              tc::umma_f16(acc0 + h * TN,
-                           tc::smem_desc<C::SWZ_MODE, C::SBO>(a_addr + h * (HALF * KC * 2) + kk * 32), bd, idesc,
-                           1u);
-            }
+            for (int kk = 0; kk < KC / 16; ++kk)
+              tc::umma_f16_masked(acc0 + h * TN,
+                                  tc::smem_desc<C::SWZ_MODE, C::SBO>(a_addr + h * (HALF * KC * 2) + kk * 32),
+                                  tc::smem_desc<C::SWZ_MODE, C::SBO>(b_addr + kk * 32), idesc, m[h].x, m[h].y,
+                                  m[h].z, m[h].w);
           }
           tc::umma_commit(bar_empty + 8 * stage);
         }
         if (!ok) break;
         tc::umma_commit(bar_afull + 8 * b);
+        tc::mbar_arrive(bar_iempty + 8 * ib);  // masks are read at issue
       }
     }
   } else {
-    // ================================= epilogue =================================
+    // ========================== epilogue and tile set-up ==========================
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int lrow = q * 32 + lane;
     const bool relu = (flags & TSC_CONV_RELU) != 0;
@@ -350,12 +325,59 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
     // one column tile: the bias is the same for every tile -> shared memory
     const bool bias_smem = n_col_tiles == 1;
     if (bias_smem) {
-      for (int i = tid - (NPROD + 32); i < TN; i += NEPI)
+      for (int i = tid - EPI0; i < TN; i += NEPI)
         s_bias[i] = (bias != nullptr && i < c_out) ? to_f32(__ldg(&bias[i])) : 0.f;
-      named_bar_sync(2, NEPI);
+      asm volatile("bar.sync 2, %0;" ::"r"(NEPI) : "memory");
     }
-    // zero both accumulator buffers (MMAs always accumulate; rows without a
-    // pair are masked off) and hand them to the MMA issuer: arrival #0
+
+    // Tile set-up for tile index `jt` (the jt-th tile of this CTA) into info
+    // block jt & 1: this warp's 2 x 32 rows.
+    auto setup = [&](int jt) {
+      const int64_t t = blockIdx.x + static_cast<int64_t>(jt) * gridDim.x;
+      const int ib = jt & 1;
+      int32_t* rows = rows_of(ib);
+      int32_t* orow = orow_of(ib);
+      uint32_t* lmask = lmask_of(ib);
+      const int64_t row_tile = t / n_col_tiles;
+      unsigned act = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = lrow + h * HALF;
+        const int64_t tr = row_tile * BMT + r;
+        const int o = tr < n_out ? (perm != nullptr ? __ldg(&perm[tr]) : static_cast<int>(tr)) : -1;
+        const bool row_ok = o >= 0 && o < n_out;
+        if (o >= n_out) raise_status(status, TSC_STATUS_INTERNAL);
+        orow[r] = row_ok ? o : -1;
+        int32_t j[KMAX];
+#pragma unroll
+        for (int kk = 0; kk < KMAX; ++kk) {
+          j[kk] = -1;
+          if (kk < K && row_ok) j[kk] = gmap != nullptr ? __ldg(&gmap[static_cast<int64_t>(kk) * n_out + o]) : o;
+        }
+#pragma unroll
+        for (int kk = 0; kk < KMAX; ++kk) {
+          if (kk >= K) break;
+          int v = j[kk];
+          if (v >= n_in) {
+            raise_status(status, TSC_STATUS_KEY_RANGE);
+            v = -1;
+          }
+          if (v < 0) v = -1;
+          rows[kk * BMT + r] = v;
+          const unsigned none = __ballot_sync(kFullMask, v < 0);
+          if (lane == 0) lmask[(kk * 2 + h) * 4 + q] = none;
+          act |= (none != kFullMask ? 1u : 0u) << kk;
+        }
+      }
+      if (lane == 0) reinterpret_cast<uint32_t*>(info0 + ib * Info::BYTES + Info::OFF_KMASK)[q] = act;
+      tc::mbar_arrive(bar_ifull + 8 * ib);
+    };
+
+    // first two tiles: info blocks 0 and 1 are free
+    const int64_t my_tiles = blockIdx.x < n_tiles ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    for (int jt = 0; jt < 2 && jt < my_tiles; ++jt) setup(jt);
+    // zero both accumulator buffers (MMAs always accumulate) and hand them to
+    // the MMA issuer: arrival #0
     for (int b = 0; b < NACC; ++b) {
       __syncwarp();
 #pragma unroll 1
@@ -370,17 +392,17 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
     }
     int it = 0;
     for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+      const int ib = it & 1;
       const int b = it % NACC;
       const int use = it / NACC;
       const int64_t row_tile = t / n_col_tiles;
       const int n0 = static_cast<int>(t - row_tile * n_col_tiles) * TN;
-      const bool ok1 = tc::mbar_wait(bar_tinfo + 8 * b, use & 1, deadline, s_abort, status);
-      const bool ok2 = ok1 && tc::mbar_wait(bar_afull + 8 * b, use & 1, deadline, s_abort, status);
-      if (!__all_sync(kFullMask, ok2)) break;
+      if (!__all_sync(kFullMask, tc::mbar_wait(bar_afull + 8 * b, use & 1, deadline, s_abort, status))) break;
       tc::tc_fence_after();
+      const int32_t* orow = orow_of(ib);
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
-        const int o = s_orow[b * BMT + h * HALF + lrow];
+        const int o = orow[h * HALF + lrow];
 #pragma unroll 1
         for (int c0 = 0; c0 < TN; c0 += 32) {
           float v[32];
@@ -432,6 +454,13 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
       tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(bar_aempty + 8 * b);
+      // prepare the tile two ahead in this info block once the producers and
+      // the MMA issuer have released it
+      if (it + 2 < my_tiles) {
+        if (!__all_sync(kFullMask, tc::mbar_wait(bar_iempty + 8 * ib, (it >> 1) & 1, deadline, s_abort, status)))
+          break;
+        setup(it + 2);
+      }
     }
   }
 
