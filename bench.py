@@ -234,9 +234,33 @@ def layer_table(records, peaks) -> list:
         pipe = tc if s == 2 else FP32_SIMT_TFLOPS * 1e12
         t_roof = max(byt / hbm, flops / pipe)
         rows.append(dict(kind="conv", ms=ms, n_in=r["n_in"], n_out=r["n_out"], c_in=r["c_in"], c_out=r["c_out"],
-                         pairs=P, bytes=byt, flops=flops, bound="hbm" if byt / hbm >= flops / pipe else "tensor",
+                         k_vol=r["k_vol"], elem=s, pairs=P, bytes=byt, flops=flops, bound="hbm" if byt / hbm >= flops / pipe else "tensor",
                          frac=t_roof / (ms / 1e3)))
     return rows
+
+
+def conv_kernel_name(r: dict, flags: int) -> str:
+    """Which kernel tsc_conv_forward runs for a layer (its dispatch rule)."""
+    from trispconv_b200 import _lib
+
+    c_in, c_out, k = r["c_in"], r["c_out"], r["k_vol"]
+    half = r["elem"] == 2
+    if half and not flags & _lib.CONV_FORCE_SIMT:
+        if flags & _lib.CONV_USE_TC and c_in % 64 == 0 and c_out % 32 == 0 and k <= 27 and c_out % 8 == 0:
+            return "k_conv_tcp"
+        if k <= 64 and c_out % 8 == 0 and (c_in % 8 == 0 or (c_in % 4 == 0 and c_in <= 16)):
+            return "k_conv_mma"
+    return "k_conv_simt"
+
+
+def measured_traffic(kernel: str):
+    """DRAM bytes per launch of `kernel` (read + write) from the committed ncu
+    summary profiles/traffic.json, or None."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text()).get(kernel)
+    return None if d is None else d.get("dram_bytes_per_launch")
 
 
 def run_ours(args) -> None:
@@ -314,29 +338,40 @@ def run_ours(args) -> None:
     rows = layer_table(probe.records, peaks)
     n_rows_step = len(rows) // args.steps
     step_rows = rows[:n_rows_step]
-    conv_rows = [r for r in rows if r["kind"] == "conv"]
-    conv_ms = sum(r["ms"] for r in conv_rows) / args.steps
-    conv_bytes = sum(r["bytes"] for r in conv_rows) / args.steps
-    conv_flops = sum(r["flops"] for r in conv_rows) / args.steps
-    n_conv = len(conv_rows) // args.steps
-    hbm_t = conv_bytes / (peaks["hbm_gbs"] * 1e9)
-    tc_t = conv_flops / (peaks["bf16_tflops"] * 1e12)
-    if hbm_t >= tc_t:
-        roof = {"bound": "hbm", "achieved": conv_bytes / n_conv / (conv_ms / n_conv / 1e3) / 1e9,
-                "peak": peaks["hbm_gbs"], "unit": "GB/s"}
-    else:
-        roof = {"bound": "tensor", "achieved": conv_flops / n_conv / (conv_ms / n_conv / 1e3) / 1e12,
-                "peak": peaks["bf16_tflops"], "unit": "TFLOP/s"}
-    roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["traffic"] = None
+    # the dominant conv kernel: the family with the largest total time
     from trispconv_b200.pytorch import functional as Fn
 
-    roof["kernel"] = ("k_conv_tc (tcgen05/TMEM)" if Fn.kernel_flags() & _lib.CONV_USE_TC else
-                      "k_conv_mma (mma.sync)") + " output-stationary implicit GEMM, all 12 conv layers"
-    roof["algorithmic_bytes_per_launch"] = conv_bytes / n_conv
-    roof["algorithmic_flops_per_launch"] = conv_flops / n_conv
-    roof["ms_per_launch"] = conv_ms / n_conv
+    flags = Fn.kernel_flags()
+    for r in rows:
+        if r["kind"] == "conv":
+            r["kernel"] = conv_kernel_name(r, flags)
+    conv_rows = [r for r in rows if r["kind"] == "conv"]
+    fam_ms = {}
+    for r in conv_rows:
+        fam_ms[r["kernel"]] = fam_ms.get(r["kernel"], 0.0) + r["ms"]
+    dom = max(fam_ms, key=fam_ms.get)
+    dom_rows = [r for r in conv_rows if r["kernel"] == dom]
+    n_dom = len(dom_rows)
+    dom_ms = sum(r["ms"] for r in dom_rows)
+    dom_bytes = sum(r["bytes"] for r in dom_rows)
+    dom_flops = sum(r["flops"] for r in dom_rows)
+    hbm_t = dom_bytes / (peaks["hbm_gbs"] * 1e9)
+    tc_t = dom_flops / (peaks["bf16_tflops"] * 1e12)
+    if hbm_t >= tc_t:
+        roof = {"bound": "hbm", "achieved": dom_bytes / n_dom / (dom_ms / n_dom / 1e3) / 1e9,
+                "peak": peaks["hbm_gbs"], "unit": "GB/s"}
+    else:
+        roof = {"bound": "tensor", "achieved": dom_flops / n_dom / (dom_ms / n_dom / 1e3) / 1e12,
+                "peak": peaks["bf16_tflops"], "unit": "TFLOP/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = measured_traffic(dom)
+    roof["kernel"] = dom
+    roof["launches_per_step"] = n_dom // args.steps
+    roof["algorithmic_bytes_per_launch"] = dom_bytes / n_dom
+    roof["algorithmic_flops_per_launch"] = dom_flops / n_dom
+    roof["ms_per_launch"] = dom_ms / n_dom
     roof["peak_source"] = peaks["source"]
+    roof["share_of_conv_time"] = fam_ms[dom] / sum(fam_ms.values())
 
     # ---- e2e through the public API with host buffers --------------------
     e2e_steps = max(3, min(args.steps, 20))
@@ -396,8 +431,8 @@ def run_ours(args) -> None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

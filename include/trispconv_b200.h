@@ -212,7 +212,7 @@ TSC_API int tsc_gather_from_pairs(const int64_t* pairs_in, const int64_t* pairs_
  * grouped into tiles; results do not depend on it.  16-bit dtypes with KRSC
  * weights, C_in % 8 == 0 (or C_in % 4 == 0 and C_in <= 16), C_out % 8 == 0
  * and K <= 64 run on the tensor cores (mma.sync); with TSC_CONV_USE_TC,
- * layers with C_in % 32 == 0, C_out % 32 == 0 and K <= 27 run on the
+ * layers with C_in % 64 == 0, C_out % 32 == 0 and K <= 27 run on the
  * persistent tcgen05/TMEM kernel instead.  Everything else runs on the CUDA
  * cores. */
 TSC_API int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t c_in,

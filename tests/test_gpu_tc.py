@@ -21,22 +21,24 @@ def _cloud(rng, shape, n):
 
 @pytest.fixture(params=["persistent", "one_tile_per_cta"])
 def tc_variant(request):
+    prev = Fn.kernel_flags()
     Fn.set_tc_simple(request.param != "persistent")
     yield request.param
-    Fn.set_tc_simple(False)
+    Fn.set_kernel_flags(prev)
 
 
 def _run_both(m, x_fn):
+    prev = Fn.kernel_flags()
     Fn.set_tensor_memory_path(True)
     try:
         a = m(x_fn())
     finally:
-        Fn.set_tensor_memory_path(False)
+        Fn.set_kernel_flags(prev)
     Fn.set_force_simt(True)
     try:
         b = m(x_fn())
     finally:
-        Fn.set_force_simt(False)
+        Fn.set_kernel_flags(prev)
     torch.cuda.synchronize()
     return a, b
 
@@ -85,12 +87,13 @@ def test_tc_vs_oracle_and_relu(cuda, tc_variant):
         m.bias.copy_(torch.from_numpy(b))
     m = m.half()
     seq = spconv.SparseSequential(m, torch.nn.ReLU())
+    prev = Fn.kernel_flags()
     Fn.set_tensor_memory_path(True)
     try:
         y = seq(spconv.SparseConvTensor(torch.from_numpy(f).to(cuda).half(), torch.from_numpy(idx).to(cuda),
                                         shape, 1))
     finally:
-        Fn.set_tensor_memory_path(False)
+        Fn.set_kernel_flags(prev)
     assert_close_rel(np_(y.features.float()), ref.features, 1e-2, "tcgen05 SubM + fused ReLU")
     from trispconv_b200 import _lib
 

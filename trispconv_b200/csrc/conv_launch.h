@@ -50,14 +50,16 @@ inline bool tc_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
   return w_krsc && K <= kMmaKMax && c_in % 8 == 0 && c_out % 8 == 0;
 }
 
-// persistent tcgen05 path (TMA gathers): additionally C_in % 32 == 0,
-// C_out % 32 == 0 and K <= 27, so that channel chunks (32 or 64) and column
-// tiles (32..256) divide the tensors exactly and no TMA box reaches outside
-// them.  32-byte feature rows (C_in = 16) and N = 16 tiles are not built: that
-// configuration made an illegal memory access on a 280k-row map although
-// every coordinate it issued was checked in range.
+// persistent tcgen05 path (TMA gathers): additionally C_in % 64 == 0,
+// C_out % 32 == 0 and K <= 27, so that channel chunks (64) and column tiles
+// (32..256) divide the tensors exactly and no TMA box reaches outside them.
+// Measured on the config-3 maps, 64-channel rows are where the TMA gather
+// beats the mma.sync kernel (32-channel layers run faster on mma.sync).
+// 32-byte feature rows (C_in = 16) and N = 16 tiles are not built at all:
+// that configuration made an illegal memory access on a 280k-row map
+// although every coordinate it issued was checked in range.
 inline bool tcp_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
-  return tc_eligible(dtype, w_krsc, c_in, c_out, K) && c_in % 32 == 0 && c_out % 32 == 0 && K <= kPersistentKMax;
+  return tc_eligible(dtype, w_krsc, c_in, c_out, K) && c_in % 64 == 0 && c_out % 32 == 0 && K <= kPersistentKMax;
 }
 
 int launch_mma_f16(const ConvArgs& a);

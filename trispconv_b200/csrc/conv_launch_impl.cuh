@@ -178,11 +178,8 @@ template <typename T, int TN>
 int launch_tcp_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                   const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
                   const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
-  // KC (64 or 32) divides c_in (tcp_eligible): every feature and weight box lies inside its tensor
-  if (c_in % 64 == 0)
-    return launch_tcp_cfg<T, TN, 64>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                     flags, status, stream);
-  return launch_tcp_cfg<T, TN, 32>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
+  // KC = 64 divides c_in (tcp_eligible): every feature and weight box lies inside its tensor
+  return launch_tcp_cfg<T, TN, 64>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
                                    flags, status, stream);
 }
 

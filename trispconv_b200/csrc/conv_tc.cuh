@@ -80,9 +80,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: false on timeout (kWaitNs after the wait began) or when
-// another role aborted.  The `deadline` argument is unused and kept for the
-// call sites' symmetry.
+// try_wait that may suspend the thread for up to `hint_ns` (it resumes as
+// soon as the phase completes).  A suspended waiter issues no instructions,
+// so waiting roles do not take issue slots from the warps doing work on the
+// same SM sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t kSuspendNs = 50000;  // upper bound of one suspension
+
+// Bounded wait: false on timeout (about kWaitCycles after the wait began) or
+// when another role aborted.  The `deadline` argument is unused and kept for
+// the call sites' symmetry.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long deadline,
                                           volatile int* abort_flag, int64_t* status) {
   (void)deadline;
@@ -90,7 +106,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
   // SM cycle counter (cheap to read, unlike %globaltimer): ~2 s at 2 GHz.
   const long long start = clock64();
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, kSuspendNs)) return true;
     if (*abort_flag) return false;
     if (clock64() - start > kWaitCycles) {
       raise_status(status, TSC_STATUS_WAIT_TIMEOUT);

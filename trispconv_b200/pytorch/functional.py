@@ -19,8 +19,10 @@ SUPPORTED_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 # TRISPCONV_B200_FORCE_SIMT=1 routes every conv to the CUDA-core kernel (A/B
 # measurements and tests of both kernels on the same inputs).
 _FORCE_FLAGS = L.CONV_FORCE_SIMT if os.environ.get("TRISPCONV_B200_FORCE_SIMT", "0") == "1" else 0
-# TRISPCONV_B200_TC=1 routes 16-bit convs with C_in % 8 == 0 to the tcgen05 kernel.
-if os.environ.get("TRISPCONV_B200_TC", "0") == "1":
+# 16-bit layers whose shapes the persistent tcgen05 kernel takes run on it
+# (the others on mma.sync); TRISPCONV_B200_TC=0 keeps every 16-bit layer on
+# mma.sync (A/B measurements).
+if os.environ.get("TRISPCONV_B200_TC", "1") != "0":
     _FORCE_FLAGS |= L.CONV_USE_TC
 
 
@@ -44,6 +46,12 @@ def set_tc_simple(on: bool) -> None:
 
 def kernel_flags() -> int:
     return _FORCE_FLAGS
+
+
+def set_kernel_flags(flags: int) -> None:
+    """Restores a value returned by kernel_flags()."""
+    global _FORCE_FLAGS
+    _FORCE_FLAGS = int(flags)
 
 
 def kernel_map_for(indice_data: IndiceData, n_out: int, device: torch.device) -> KernelMap:
