@@ -253,14 +253,17 @@ def conv_kernel_name(r: dict, flags: int) -> str:
     return "k_conv_simt"
 
 
-def measured_traffic(kernel: str):
-    """DRAM bytes per launch of `kernel` (read + write) from the committed ncu
-    summary profiles/traffic.json, or None."""
+def measured_traffic(kernel: str, algorithmic_bytes_per_launch: float):
+    """DRAM bytes (read + write) per launch of `kernel`: the launch captured in
+    the committed ncu summary profiles/traffic.json, scaled to this run's
+    average launch by algorithmic bytes.  None when no capture exists."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None
     d = json.loads(p.read_text()).get(kernel)
-    return None if d is None else d.get("dram_bytes_per_launch")
+    if d is None:
+        return None
+    return d["dram_bytes_per_launch_captured"] / d["algorithmic_bytes_captured"] * algorithmic_bytes_per_launch
 
 
 def run_ours(args) -> None:
@@ -364,7 +367,9 @@ def run_ours(args) -> None:
         roof = {"bound": "tensor", "achieved": dom_flops / n_dom / (dom_ms / n_dom / 1e3) / 1e12,
                 "peak": peaks["bf16_tflops"], "unit": "TFLOP/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["traffic"] = measured_traffic(dom)
+    roof["traffic"] = measured_traffic(dom, dom_bytes / n_dom)
+    roof["traffic_note"] = ("ncu DRAM read+write of one captured launch (profiles/traffic.json), scaled by "
+                            "algorithmic bytes to the average launch")
     roof["kernel"] = dom
     roof["launches_per_step"] = n_dom // args.steps
     roof["algorithmic_bytes_per_launch"] = dom_bytes / n_dom
@@ -380,10 +385,13 @@ def run_ours(args) -> None:
     e_start = torch.cuda.Event(enable_timing=True)
     e_end = torch.cuda.Event(enable_timing=True)
     e2e_ms = 0.0
+    e2e_list = []
+    host_list = []
     d2h = 0
     res_h = None
     for i in range(e2e_steps + 1):  # iteration 0 sizes the pinned result buffer (untimed)
         flush.fill_(float(i))
+        h0 = time.perf_counter()
         e_start.record()
         f = feats_h.to(dev, non_blocking=True)
         ix = idx_h.to(dev, non_blocking=True)
@@ -395,6 +403,8 @@ def run_ours(args) -> None:
         e_end.synchronize()
         if i > 0:
             e2e_ms += e_start.elapsed_time(e_end)
+            e2e_list.append(round(e_start.elapsed_time(e_end), 4))
+            host_list.append(round((time.perf_counter() - h0) * 1e3, 4))
         d2h = res_h.numel() * res_h.element_size()
     t = torch.tensor([e2e_ms / e2e_steps], dtype=torch.float64, device=dev)
     if ws > 1:
@@ -414,7 +424,7 @@ def run_ours(args) -> None:
                        "spatial_shape": wl.spatial_shape, "layers": 12, "parallelism": f"batch-shard x{ws}",
                        "l2": "flushed between steps (256 MiB write outside the timed events)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": float(t.item())},
+                    "ms_per_step": float(t.item()), "step_ms": e2e_list, "host_ms": host_list},
             "gpu_launches": launches,
             "roofline": roof,
             "cpu_baseline": cpu,

@@ -230,6 +230,18 @@ TSC_API int tsc_to_dense(const void* features, int32_t dtype, const int32_t* ind
                  int32_t batch, const int32_t* shape3, int32_t channels_first,
                  void* out, int64_t* status, void* stream);
 
+/* ---- row order for the convolution kernels --------------------------------
+ * No counterpart in the reference (its CPU path has no tiles).  Groups the
+ * output rows of a gather map by neighbour mask (bit k set when
+ * gather_map[k][o] >= 0), masks ascending, so that the rows of a conv tile
+ * share their kernel offsets; writes a permutation of [0, n_out) to
+ * row_order, to be passed to tsc_conv_forward.  Convolution results do not
+ * depend on it.  1 <= K <= 32.  More than 16384 distinct masks leave the
+ * identity order. */
+TSC_API size_t tsc_row_order_workspace(int64_t n_out);
+TSC_API int tsc_row_order(const int32_t* gather_map, int32_t k_vol, int64_t n_out, void* workspace,
+                  size_t workspace_bytes, int32_t* row_order, int64_t* status, void* stream);
+
 /* ---- allocation-free submanifold kernel map ------------------------------
  * No counterpart in the reference: an addition for callers that cannot
  * allocate device memory when they build a map (a host that owns a fixed

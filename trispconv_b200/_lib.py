@@ -95,6 +95,8 @@ _SIGNATURES = {
     "tsc_conv_forward": (ctypes.c_int, [_P, c_int32, c_int64, c_int32, _P, c_int32, _P, _P, _P, c_int32,
                                         c_int64, c_int32, _P, c_int64, _P, _P, c_int32, _P, _P]),
     "tsc_to_dense": (ctypes.c_int, [_P, c_int32, _P, c_int64, c_int32, c_int32, _P, c_int32, _P, _P, _P]),
+    "tsc_row_order_workspace": (c_size_t, [c_int64]),
+    "tsc_row_order": (ctypes.c_int, [_P, c_int32, c_int64, _P, c_size_t, _P, _P, _P]),
     "tsc_subm_kmap_noalloc_max_voxels": (c_int64, []),
     "tsc_subm_kmap_noalloc": (ctypes.c_int, [_P, c_int64, POINTER(Geometry), _P, _P, _P, _P]),
 }

@@ -265,7 +265,8 @@ int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t 
   }
   if (!force_simt && mma_eligible(dtype, w_krsc, c_in, c_out, k_vol))
     return f16 ? launch_mma_f16(a) : launch_mma_bf16(a);
-  TSC_CHECK_ARG(row_order == nullptr, "row_order is only supported by the tensor-core path");
+  // the CUDA-core kernel walks rows in index order; results do not depend on
+  // the row order, so it is ignored here
   switch (dtype) {
     case TSC_F32:
       return launch_simt<float>(features, n_in, c_in, weight, weight_layout == TSC_W_KRSC, bias, gather_map, k_vol, n_out, c_out, overflow,

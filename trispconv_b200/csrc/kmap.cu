@@ -150,9 +150,88 @@ k_subm_query(const int4* __restrict__ idx, int64_t n, GeoDev g,
   if (threadIdx.x == 0 && cnt) atomicAdd(&meta[TSC_META_COUNTS + k], static_cast<unsigned long long>(cnt));
 }
 
+// One thread per row i for all K offsets (K <= kRowQueryKMax): the row's
+// coordinates are read once, the x-neighbour lookups of one (dz, dy) hit the
+// same hash cache line (the hash keeps the low 3 key bits), and the writes
+// gather_map[k][i] stay coalesced across the warp.  pair_num[k] is reduced
+// per warp (ballot) and per block (shared memory) before one atomic per
+// offset and block.
+constexpr int kRowQueryKMax = 128;
+
+__global__ void __launch_bounds__(kThreads)
+k_subm_query_rows(const int4* __restrict__ idx, int64_t n, GeoDev g,
+                  const unsigned long long* __restrict__ table, int log2cap,
+                  int32_t* __restrict__ gmap, unsigned long long* __restrict__ meta) {
+  __shared__ unsigned s_cnt[kRowQueryKMax];
+  const int K = g.kD * g.kH * g.kW;
+  for (int t = threadIdx.x; t < K; t += blockDim.x) s_cnt[t] = 0u;
+  __syncthreads();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const bool row = i < n;
+  int4 c = make_int4(-1, 0, 0, 0);
+  if (row) c = __ldg(&idx[i]);
+  const bool b_ok = row && static_cast<unsigned>(c.x) < static_cast<unsigned>(g.B);
+  const int lane = threadIdx.x & 31;
+  int k = 0;
+  for (int kz = 0; kz < g.kD; ++kz) {
+    const int nz = c.y + (kz - g.kD / 2) * g.dz;
+    for (int ky = 0; ky < g.kH; ++ky) {
+      const int ny = c.z + (ky - g.kH / 2) * g.dy;
+      const bool zy_ok = b_ok && static_cast<unsigned>(nz) < static_cast<unsigned>(g.D) &&
+                         static_cast<unsigned>(ny) < static_cast<unsigned>(g.H);
+      for (int kx = 0; kx < g.kW; ++kx, ++k) {
+        const int nx = c.w + (kx - g.kW / 2) * g.dx;
+        int found = -1;
+        if (zy_ok && static_cast<unsigned>(nx) < static_cast<unsigned>(g.W))
+          found = hash_lookup(table, log2cap, cell_key(c.x, nz, ny, nx, g.D, g.H, g.W));
+        if (row) gmap[static_cast<int64_t>(k) * n + i] = found;
+        const unsigned hits = __ballot_sync(kFullMask, found >= 0);
+        if (lane == 0 && hits) atomicAdd(&s_cnt[k], static_cast<unsigned>(__popc(hits)));
+      }
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < K; t += blockDim.x)
+    if (s_cnt[t]) atomicAdd(&meta[TSC_META_COUNTS + t], static_cast<unsigned long long>(s_cnt[t]));
+}
+
+// Builds gather_map and pair_num from a filled hash table (both the
+// workspace and the allocation-free entry points).
+int launch_subm_query(const int4* idx, int64_t n, const GeoDev& g, const unsigned long long* table, int log2cap,
+                      int32_t* gmap, int64_t* meta, cudaStream_t stream) {
+  const int K = g.kD * g.kH * g.kW;
+  const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
+  if (K <= kRowQueryKMax) {
+    k_subm_query_rows<<<grid, kThreads, 0, stream>>>(idx, n, g, table, log2cap, gmap,
+                                                     reinterpret_cast<unsigned long long*>(meta));
+    TSC_LAUNCH_CHECK("k_subm_query_rows");
+  } else {
+    k_subm_query<<<dim3(grid, K), kThreads, 0, stream>>>(idx, n, g, table, log2cap, gmap,
+                                                         reinterpret_cast<unsigned long long*>(meta));
+    TSC_LAUNCH_CHECK("k_subm_query");
+  }
+  return TSC_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Strided: occupancy bitmap over the output grid
 // ---------------------------------------------------------------------------
+
+// o = c / s when c >= 0 is a multiple of s and c / s < lim (the candidate
+// output position of one dimension); strides 1 and 2 avoid the division.
+__device__ __forceinline__ bool exact_div(int c, int s, int lim, int& o) {
+  if (c < 0) return false;
+  if (s == 1) {
+    o = c;
+  } else if (s == 2) {
+    if (c & 1) return false;
+    o = c >> 1;
+  } else {
+    if (c % s) return false;
+    o = c / s;
+  }
+  return o < lim;
+}
 
 // Per input row, walks the K offsets in reference order (indices.py:177-187):
 // c = i + p - k*d is a valid output position iff c >= 0, c % s == 0 and
@@ -179,20 +258,18 @@ k_strided_mark(const int4* __restrict__ idx, int64_t n, GeoDev g, uint32_t* __re
   bool any = false;
   int k = 0;
   for (int kz = 0; kz < g.kD; ++kz) {
-    const int cz = c.y + g.pz - kz * g.dz;
-    const bool vz = cz >= 0 && (cz % g.sz) == 0 && (cz / g.sz) < g.oD;
-    const int oz = vz ? cz / g.sz : 0;
+    int oz = 0;
+    const bool vz = exact_div(c.y + g.pz - kz * g.dz, g.sz, g.oD, oz);
     for (int ky = 0; ky < g.kH; ++ky) {
-      const int cy = c.z + g.py - ky * g.dy;
-      const bool vy = vz && cy >= 0 && (cy % g.sy) == 0 && (cy / g.sy) < g.oH;
-      const int oy = vy ? cy / g.sy : 0;
+      int oy = 0;
+      const bool vy = vz && exact_div(c.z + g.py - ky * g.dy, g.sy, g.oH, oy);
       for (int kx = 0; kx < g.kW; ++kx, ++k) {
-        const int cx = c.w + g.px - kx * g.dx;
-        const bool v = active && vy && cx >= 0 && (cx % g.sx) == 0 && (cx / g.sx) < g.oW;
+        int ox = 0;
+        const bool v = active && vy && exact_div(c.w + g.px - kx * g.dx, g.sx, g.oW, ox);
         const unsigned b = __ballot_sync(kFullMask, v);
         if (v) {
           // Lanes that hit the same bitmap word combine their bits; one atomic per word.
-          const uint32_t lin = cell_key(c.x, oz, oy, cx / g.sx, g.oD, g.oH, g.oW);
+          const uint32_t lin = cell_key(c.x, oz, oy, ox, g.oD, g.oH, g.oW);
           const uint32_t word = lin >> 5;
           const unsigned same = __match_any_sync(b, word);
           const unsigned bits = __reduce_or_sync(same, 1u << (lin & 31u));
@@ -343,19 +420,17 @@ k_strided_pairs(const int4* __restrict__ idx, int64_t n, GeoDev g,
   const bool active = in_grid(c, g.B, g.D, g.H, g.W);
   int k = 0;
   for (int kz = 0; kz < g.kD; ++kz) {
-    const int cz = c.y + g.pz - kz * g.dz;
-    const bool vz = active && cz >= 0 && (cz % g.sz) == 0 && (cz / g.sz) < g.oD;
-    const int oz = vz ? cz / g.sz : 0;
+    int oz = 0;
+    const bool vz = active && exact_div(c.y + g.pz - kz * g.dz, g.sz, g.oD, oz);
     for (int ky = 0; ky < g.kH; ++ky) {
-      const int cy = c.z + g.py - ky * g.dy;
-      const bool vy = vz && cy >= 0 && (cy % g.sy) == 0 && (cy / g.sy) < g.oH;
-      const int oy = vy ? cy / g.sy : 0;
+      int oy = 0;
+      const bool vy = vz && exact_div(c.z + g.py - ky * g.dy, g.sy, g.oH, oy);
       for (int kx = 0; kx < g.kW; ++kx, ++k) {
-        const int cx = c.w + g.px - kx * g.dx;
-        const bool v = vy && cx >= 0 && (cx % g.sx) == 0 && (cx / g.sx) < g.oW;
+        int ox = 0;
+        const bool v = vy && exact_div(c.w + g.px - kx * g.dx, g.sx, g.oW, ox);
         int o = -1;
         if (v) {
-          const uint32_t lin = cell_key(c.x, oz, oy, cx / g.sx, g.oD, g.oH, g.oW);
+          const uint32_t lin = cell_key(c.x, oz, oy, ox, g.oD, g.oH, g.oW);
           const uint32_t w = lin >> 5;
           o = static_cast<int>(__ldg(&word_prefix[w]) +
                                __popc(__ldg(&bitmap[w]) & ((1u << (lin & 31u)) - 1u)));
@@ -687,10 +762,7 @@ int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo, vo
   const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
   k_hash_build<<<grid, kThreads, 0, stream>>>(idx, n, g.B, g.D, g.H, g.W, table, log2cap, status);
   TSC_LAUNCH_CHECK("k_hash_build");
-  k_subm_query<<<dim3(grid, K), kThreads, 0, stream>>>(idx, n, g, table, log2cap, gather_map,
-                                                       reinterpret_cast<unsigned long long*>(meta));
-  TSC_LAUNCH_CHECK("k_subm_query");
-  return TSC_OK;
+  return launch_subm_query(idx, n, g, table, log2cap, gather_map, meta, stream);
 }
 
 size_t tsc_strided_kmap_workspace(const tsc_geometry* geo) {
@@ -1036,10 +1108,7 @@ int tsc_subm_kmap_noalloc(const int32_t* indices, int64_t n, const tsc_geometry*
   const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
   k_hash_build<<<grid, kThreads, 0, stream>>>(idx, n, g.B, g.D, g.H, g.W, table, log2cap, status);
   TSC_LAUNCH_CHECK("k_hash_build");
-  k_subm_query<<<dim3(grid, K), kThreads, 0, stream>>>(idx, n, g, table, log2cap, gather_map,
-                                                       reinterpret_cast<unsigned long long*>(meta));
-  TSC_LAUNCH_CHECK("k_subm_query");
-  return TSC_OK;
+  return launch_subm_query(idx, n, g, table, log2cap, gather_map, meta, stream);
 }
 
 }  // extern "C"

@@ -12,7 +12,7 @@ from typing import Optional
 import torch
 
 from trispconv_b200 import _lib as L
-from trispconv_b200.pytorch.indices import IndiceData, KernelMap, kmap_from_pairs
+from trispconv_b200.pytorch.indices import IndiceData, KernelMap, build_row_order, kmap_from_pairs
 
 SUPPORTED_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 
@@ -24,6 +24,20 @@ _FORCE_FLAGS = L.CONV_FORCE_SIMT if os.environ.get("TRISPCONV_B200_FORCE_SIMT", 
 # mma.sync (A/B measurements).
 if os.environ.get("TRISPCONV_B200_TC", "1") != "0":
     _FORCE_FLAGS |= L.CONV_USE_TC
+
+
+# TRISPCONV_B200_ROW_ORDER=1 makes 16-bit convolutions over maps with at
+# least ROW_ORDER_MIN_ROWS output rows group their rows by neighbour mask
+# first (tsc_row_order, once per kernel map).  Off by default: on the
+# config-3 backbone it did not shorten the conv kernels and the ordering
+# itself cost 0.1-0.2 ms per map.
+ROW_ORDER_MIN_ROWS = 16384
+_ROW_ORDER = os.environ.get("TRISPCONV_B200_ROW_ORDER", "0") == "1"
+
+
+def set_row_order(on: bool) -> None:
+    global _ROW_ORDER
+    _ROW_ORDER = bool(on)
 
 
 def set_force_simt(on: bool) -> None:
@@ -90,6 +104,9 @@ def conv_launch(features: torch.Tensor, weight: torch.Tensor, weight_layout: int
         cap, k_vol = 0, 1
     else:
         gather, overflow, meta, cap, k_vol = km.gather, km.overflow, km.meta, km.overflow_cap, km.k_vol
+        if (_ROW_ORDER and km.row_order is None and gather is not None and dtype != torch.float32
+                and k_vol <= 32 and n_out >= ROW_ORDER_MIN_ROWS and km.n_out == n_out):
+            km.row_order = build_row_order(km)
         order = km.row_order
     if weight_layout == L.W_KCC and dtype != torch.float32:
         # The tensor-core kernels read B as (C_out, K, C_in) rows: transpose the

@@ -75,6 +75,20 @@ class KernelMap:
         self.row_order = row_order
 
 
+def build_row_order(km: "KernelMap") -> torch.Tensor:
+    """Output rows of `km` grouped by neighbour mask (tsc_row_order), for the
+    tensor-core conv kernels; cached on the map by the caller."""
+    dev = km.device
+    lib = L.load()
+    order = torch.empty(km.n_out, dtype=torch.int32, device=dev)
+    ws = L.workspace(lib.tsc_row_order_workspace(km.n_out), dev)
+    with torch.cuda.device(dev):
+        L.check(lib.tsc_row_order(km.gather.data_ptr(), km.k_vol, km.n_out, ws.data_ptr(), ws.numel(),
+                                  order.data_ptr(), L.status_word(dev).data_ptr(), L.stream_ptr(dev)),
+                "tsc_row_order")
+    return order
+
+
 class IndiceData:
     """Kernel map of one convolution (indices.py:10-23).
 
