@@ -214,13 +214,16 @@ TSC_API int tsc_gather_from_pairs(const int64_t* pairs_in, const int64_t* pairs_
  * and K <= 64 run on the tensor cores (mma.sync); with TSC_CONV_USE_TC,
  * layers with C_in % 64 == 0, C_out % 32 == 0 and K <= 27 run on the
  * persistent tcgen05/TMEM kernel instead.  Everything else runs on the CUDA
- * cores. */
+ * cores.  tile_counter (NULL allowed) is one device uint32 through which the
+ * persistent kernel's CTAs take tiles dynamically (the call zeroes it on
+ * `stream`); calls that may run concurrently need distinct counters.  With
+ * NULL, tiles are dealt round robin. */
 TSC_API int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t c_in,
                      const void* weight, int32_t weight_layout, const void* bias,
                      const int32_t* gather_map, const int32_t* row_order,
                      int32_t k_vol, int64_t n_out, int32_t c_out,
                      const int32_t* overflow, int64_t overflow_cap, const int64_t* meta,
-                     void* out, int32_t flags, int64_t* status, void* stream);
+                     void* out, int32_t flags, int64_t* status, uint32_t* tile_counter, void* stream);
 
 /* ---- dense scatter ---------------------------------------------------------
  * SparseConvTensor.dense() (tensor.py:72-99): writes features into a zeroed

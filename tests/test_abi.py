@@ -73,10 +73,10 @@ def test_host_side_argument_checks(lib):
                            ctypes.addressof(s), None)
     assert rc == L.TSC_ERR_GRID_TOO_LARGE
     rc = lib.tsc_conv_forward(None, 0, 10, 0, None, 0, None, None, None, 27, 10, 8, None, 0, None, None, 0,
-                              ctypes.addressof(s), None)
+                              ctypes.addressof(s), None, None)
     assert rc == L.TSC_ERR_INVALID_ARG
     rc = lib.tsc_conv_forward(None, 0, 10, 4, None, 0, None, None, None, 27, 10, 8, None, 0, None, None, 0,
-                              ctypes.addressof(s), None)
+                              ctypes.addressof(s), None, None)
     assert rc == L.TSC_ERR_INVALID_ARG and "identity" in L.last_error()
     rc = lib.tsc_pairs_materialize(None, 27, 10, 7, None, None, None, 5, None, 0, None, None)
     assert rc == L.TSC_ERR_INVALID_ARG

@@ -159,3 +159,30 @@ def test_tc_remaining_tile_shapes(cuda, tc_variant, cin, cout):
     m = spconv.SubMConv3d(cin, cout, 3).to(cuda).half()
     a, b = _run_both(m, lambda: spconv.SparseConvTensor(f, idx, shape, 1))
     _assert_same(a, b, torch.float16, f"{cin}->{cout}")
+
+
+def test_tcp_dynamic_and_round_robin_schedules_agree(cuda):
+    """The persistent kernel hands out tiles through a device counter; with
+    NULL it deals them round robin.  Both must give identical outputs."""
+    from trispconv_b200 import _lib as L
+    from trispconv_b200.pytorch.indices import generate_subm_indice_pairs
+
+    rng = np.random.default_rng(9)
+    shape = (60, 60, 60)
+    n = 200_000
+    idx = torch.from_numpy(_cloud(rng, shape, n)).to(cuda)
+    km = generate_subm_indice_pairs(idx, shape, 1, 3)._kmap
+    f = torch.from_numpy(rng.standard_normal((n, 64)).astype(np.float32)).to(cuda).half()
+    w = (torch.randn(64, 3, 3, 3, 64, device=cuda) * 0.05).half()
+    outs = []
+    for counter in (L.tile_counter(cuda), None):
+        out = torch.empty(n, 64, dtype=torch.half, device=cuda)
+        rc = L.load().tsc_conv_forward(f.data_ptr(), L.DTYPE_CODE[torch.float16], n, 64, w.data_ptr(), L.W_KRSC,
+                                       None, km.gather.data_ptr(), None, 27, n, 64, None, 0, km.meta.data_ptr(),
+                                       out.data_ptr(), L.CONV_USE_TC, L.status_word(cuda).data_ptr(),
+                                       None if counter is None else counter.data_ptr(), L.stream_ptr(cuda))
+        L.check(rc, "tsc_conv_forward")
+        outs.append(out)
+    torch.cuda.synchronize()
+    L.check_device_status(cuda)
+    assert torch.equal(outs[0], outs[1])

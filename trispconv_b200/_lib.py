@@ -93,7 +93,7 @@ _SIGNATURES = {
                                              _P, _P]),
     "tsc_gather_from_pairs": (ctypes.c_int, [_P, _P, _P, c_int32, c_int64, _P, _P, c_int64, _P, _P, _P]),
     "tsc_conv_forward": (ctypes.c_int, [_P, c_int32, c_int64, c_int32, _P, c_int32, _P, _P, _P, c_int32,
-                                        c_int64, c_int32, _P, c_int64, _P, _P, c_int32, _P, _P]),
+                                        c_int64, c_int32, _P, c_int64, _P, _P, c_int32, _P, _P, _P]),
     "tsc_to_dense": (ctypes.c_int, [_P, c_int32, _P, c_int64, c_int32, c_int32, _P, c_int32, _P, _P, _P]),
     "tsc_row_order_workspace": (c_size_t, [c_int64]),
     "tsc_row_order": (ctypes.c_int, [_P, c_int32, c_int64, _P, c_size_t, _P, _P, _P]),
@@ -179,6 +179,20 @@ def status_word(device: torch.device) -> torch.Tensor:
     if t is None:
         t = torch.zeros(1, dtype=torch.int64, device=torch.device("cuda", idx))
         _status[idx] = t
+    return t
+
+
+_counters: dict = {}
+
+
+def tile_counter(device: torch.device) -> torch.Tensor:
+    """Per-device uint32 through which the persistent conv kernel hands out
+    tiles (zeroed by every conv call on its stream)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _counters.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _counters[idx] = t
     return t
 
 

@@ -231,7 +231,7 @@ extern "C" {
 int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t c_in, const void* weight,
                      int32_t weight_layout, const void* bias, const int32_t* gather_map, const int32_t* row_order, int32_t k_vol, int64_t n_out,
                      int32_t c_out, const int32_t* overflow, int64_t overflow_cap, const int64_t* meta,
-                     void* out, int32_t flags, int64_t* status, void* stream_) {
+                     void* out, int32_t flags, int64_t* status, uint32_t* tile_counter, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   TSC_CHECK_ARG(c_in > 0 && c_out > 0, "channel counts must be positive (c_in=%d, c_out=%d)", c_in, c_out);
   TSC_CHECK_ARG(k_vol > 0 && k_vol <= 4096, "kernel volume %d out of range", k_vol);
@@ -253,7 +253,7 @@ int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t 
   const int w_krsc = weight_layout == TSC_W_KRSC;
   const bool force_simt = (flags & TSC_CONV_FORCE_SIMT) != 0;
   const ConvArgs a{features, n_in, c_in, weight, bias, gather_map, row_order, k_vol, n_out, c_out,
-                   overflow, overflow_cap, meta, out, flags, status, stream};
+                   overflow, overflow_cap, meta, out, flags, status, tile_counter, stream};
   const bool f16 = dtype == TSC_F16;
   if (!force_simt && (flags & TSC_CONV_USE_TC) != 0) {
     // the one-tile-per-CTA kernel only on request (testing); otherwise the

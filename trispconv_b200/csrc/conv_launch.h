@@ -27,6 +27,7 @@ struct ConvArgs {
   void* out;
   int flags;
   int64_t* status;
+  uint32_t* tile_counter;  // persistent kernel: dynamic tile hand-out (NULL = round robin)
   cudaStream_t stream;
 };
 

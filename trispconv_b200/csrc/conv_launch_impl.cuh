@@ -152,7 +152,8 @@ int encode_maps(const T* f, int64_t n_in, int c_in, const T* w, int K, int c_out
 template <typename T, int TN, int KC>
 int launch_tcp_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                    const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                   const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+                   const int64_t* meta, T* out, int flags, int64_t* status, uint32_t* tile_counter,
+                   cudaStream_t stream) {
   using C = tcp::Cfg<TN, KC>;
   auto kern = tcp::k_conv_tcp<T, TN, KC>;
   CUtensorMap mf, mw;
@@ -167,9 +168,10 @@ int launch_tcp_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias
   }
   const int64_t tiles = ceil_div(n_out, tcp::BMT) * ceil_div(c_out, TN);
   const int64_t grid = tiles < sm_count() ? tiles : sm_count();
+  if (tile_counter != nullptr) TSC_CUDA(cudaMemsetAsync(tile_counter, 0, sizeof(uint32_t), stream));
   kern<<<static_cast<unsigned>(grid), tcp::NT, C::TOTAL, stream>>>(mf, mw, f, n_in, c_in, w, bias, gmap, perm, K,
                                                                   n_out, c_out, ovf, ovf_cap, meta, out, flags,
-                                                                  status);
+                                                                  status, tile_counter);
   TSC_LAUNCH_CHECK("k_conv_tcp");
   return TSC_OK;
 }
@@ -177,16 +179,18 @@ int launch_tcp_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias
 template <typename T, int TN>
 int launch_tcp_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                   const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                  const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+                  const int64_t* meta, T* out, int flags, int64_t* status, uint32_t* tile_counter,
+                   cudaStream_t stream) {
   // KC = 64 divides c_in (tcp_eligible): every feature and weight box lies inside its tensor
   return launch_tcp_cfg<T, TN, 64>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                   flags, status, stream);
+                                   flags, status, tile_counter, stream);
 }
 
 template <typename T>
 int launch_tcp(const void* F, int64_t n_in, int c_in, const void* W, const void* bias, const int32_t* gmap,
                const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-               const int64_t* meta, void* out, int flags, int64_t* status, cudaStream_t stream) {
+               const int64_t* meta, void* out, int flags, int64_t* status, uint32_t* tile_counter,
+               cudaStream_t stream) {
   const T* f = static_cast<const T*>(F);
   const T* w = static_cast<const T*>(W);
   const T* b = static_cast<const T*>(bias);
@@ -194,15 +198,15 @@ int launch_tcp(const void* F, int64_t n_in, int c_in, const void* W, const void*
   // the largest UMMA N that divides c_out (tcp_eligible: c_out % 32 == 0)
   if (c_out % 256 == 0)
     return launch_tcp_tn<T, 256>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                 status, stream);
+                                 status, tile_counter, stream);
   if (c_out % 128 == 0)
     return launch_tcp_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                 status, stream);
+                                 status, tile_counter, stream);
   if (c_out % 64 == 0)
     return launch_tcp_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                                status, stream);
+                                 status, tile_counter, stream);
   return launch_tcp_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
-                              status, stream);
+                                 status, tile_counter, stream);
 }
 
 

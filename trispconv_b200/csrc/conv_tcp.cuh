@@ -82,7 +82,8 @@ struct Info {
   static constexpr int OFF_OROW = OFF_ROWS + ROWS;
   static constexpr int OFF_LMASK = OFF_OROW + OROW;
   static constexpr int OFF_KMASK = OFF_LMASK + LMASK;
-  static constexpr int BYTES = (OFF_KMASK + KMASK + 127) / 128 * 128;
+  static constexpr int OFF_TILE = OFF_KMASK + KMASK;  // int32 tile index, -1 = no more tiles
+  static constexpr int BYTES = (OFF_TILE + 4 + 127) / 128 * 128;
 };
 
 template <int TN, int KC>
@@ -95,8 +96,8 @@ struct Cfg {
   // stages start on 1024-byte boundaries (swizzle atoms are address based)
   static constexpr int STAGE = (A_BYTES + B_BYTES + 1023) / 1024 * 1024;
   // control block: full[NS], empty[NS], ifull[2], iempty[2], afull[2],
-  // aempty[2], tmem addr, abort
-  static constexpr int CTRL_MAX = 16 * 16 + 64 + 16;
+  // aempty[2], tidx[2], tmem addr, abort, tile index hand-off[2]
+  static constexpr int CTRL_MAX = 16 * 16 + 80 + 16;
   static constexpr int BIAS = 256 * 4;
   static constexpr int FIXED = 1024 /*alignment slack*/ + 2 * Info::BYTES + BIAS + (CTRL_MAX + 127) / 128 * 128;
   static constexpr int NS_FIT = (SMEM_MAX - FIXED) / STAGE;
@@ -108,9 +109,11 @@ struct Cfg {
   static constexpr int OFF_IEMPTY = OFF_IFULL + 16;
   static constexpr int OFF_AFULL = OFF_IEMPTY + 16;
   static constexpr int OFF_AEMPTY = OFF_AFULL + 16;
-  static constexpr int OFF_TMEM = OFF_AEMPTY + 16;
+  static constexpr int OFF_TIDXB = OFF_AEMPTY + 16;
+  static constexpr int OFF_TMEM = OFF_TIDXB + 16;
   static constexpr int OFF_ABORT = OFF_TMEM + 4;
-  static constexpr int CTRL = (OFF_ABORT + 4 + 127) / 128 * 128;
+  static constexpr int OFF_TIDX = OFF_ABORT + 4;    // int32[2]
+  static constexpr int CTRL = (OFF_TIDX + 8 + 127) / 128 * 128;
   static_assert(CTRL <= (CTRL_MAX + 127) / 128 * 128, "control block");
   static constexpr int OFF_INFO = PIPE + CTRL;         // from the ring base
   static constexpr int OFF_BIAS = OFF_INFO + 2 * Info::BYTES;
@@ -126,7 +129,8 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
            const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__ W,
            const T* __restrict__ bias, const int32_t* __restrict__ gmap, const int32_t* __restrict__ perm, int K,
            int64_t n_out, int c_out, const int32_t* __restrict__ ovf, int64_t ovf_cap,
-           const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status) {
+           const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status,
+           unsigned* __restrict__ tile_counter) {
   using C = Cfg<TN, KC>;
   constexpr int NS = C::NS;
   constexpr int NACC = C::NACC;
@@ -143,6 +147,8 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
   const uint32_t bar_iempty = ctrl_u32 + C::OFF_IEMPTY;
   const uint32_t bar_afull = ctrl_u32 + C::OFF_AFULL;
   const uint32_t bar_aempty = ctrl_u32 + C::OFF_AEMPTY;
+  const uint32_t bar_tidx = ctrl_u32 + C::OFF_TIDXB;
+  volatile int32_t* s_tidx = reinterpret_cast<volatile int32_t*>(ctrl + C::OFF_TIDX);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(ctrl + C::OFF_TMEM);
   volatile int* s_abort = reinterpret_cast<volatile int*>(ctrl + C::OFF_ABORT);
   unsigned char* info0 = ring + C::OFF_INFO;
@@ -154,6 +160,7 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
     const uint32_t* p = reinterpret_cast<const uint32_t*>(info0 + ib * Info::BYTES + Info::OFF_KMASK);
     return p[0] | p[1] | p[2] | p[3];
   };
+  auto tile_of = [&](int ib) { return *reinterpret_cast<const int32_t*>(info0 + ib * Info::BYTES + Info::OFF_TILE); };
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -174,6 +181,7 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
       tc::mbar_init(bar_iempty + 8 * b, NPROD / 32 + 1);  // producer warps + MMA issuer
       tc::mbar_init(bar_afull + 8 * b, 1);
       tc::mbar_init(bar_aempty + 8 * b, NEPI);
+      tc::mbar_init(bar_tidx + 8 * b, 1);
     }
     *s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -192,12 +200,13 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
   if (warp < 4) {
     // =============================== producers ===============================
     int64_t gstep = 0;  // ring position (same sequence in every producer warp)
-    int it = 0;
-    for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+    for (int it = 0;; ++it) {
       const int ib = it & 1;
       const bool ok = __all_sync(kFullMask, tc::mbar_wait(bar_ifull + 8 * ib, (it >> 1) & 1, deadline, s_abort,
                                                           status));
       if (!ok) break;
+      const int64_t t = tile_of(ib);
+      if (t < 0) break;  // no more tiles for this CTA
       const int64_t row_tile = t / n_col_tiles;
       const int n0 = static_cast<int>(t - row_tile * n_col_tiles) * TN;
       const int32_t* rows = rows_of(ib);
@@ -263,12 +272,12 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
     if (lane == 0) {
       constexpr uint32_t idesc = tc::instr_desc<T, TN>();
       int64_t gstep = 0;
-      int it = 0;
-      for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+      for (int it = 0;; ++it) {
         const int ib = it & 1;
         const int b = it % NACC;
         const int use = it / NACC;
         if (!tc::mbar_wait(bar_ifull + 8 * ib, (it >> 1) & 1, deadline, s_abort, status)) break;
+        if (tile_of(ib) < 0) break;  // no more tiles for this CTA
         unsigned rem = kmask_of(ib);
         const int steps = __popc(rem) * n_chunks;
         const uint32_t* lmask = lmask_of(ib);
@@ -330,11 +339,42 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
       asm volatile("bar.sync 2, %0;" ::"r"(NEPI) : "memory");
     }
 
-    // Tile set-up for tile index `jt` (the jt-th tile of this CTA) into info
+    // The tile of this CTA's jt-th slot: with a tile counter, the first
+    // epilogue warp takes the next tile index from it and hands it to the
+    // other three through tidx[jt & 1]; without one, tiles are dealt round
+    // robin.  -1 = no more tiles.
+    auto grab = [&](int jt) -> int64_t {
+      if (tile_counter == nullptr) {
+        const int64_t t = blockIdx.x + static_cast<int64_t>(jt) * gridDim.x;
+        return t < n_tiles ? t : -1;
+      }
+      if (warp == EPI0 / 32) {
+        int64_t t = -1;
+        if (lane == 0) {
+          const unsigned v = atomicAdd(tile_counter, 1u);
+          t = v < static_cast<uint64_t>(n_tiles) ? static_cast<int64_t>(v) : -1;
+          s_tidx[jt & 1] = static_cast<int32_t>(t);
+          tc::mbar_arrive(bar_tidx + 8 * (jt & 1));
+        }
+        return __shfl_sync(kFullMask, t, 0);
+      }
+      if (!__all_sync(kFullMask, tc::mbar_wait(bar_tidx + 8 * (jt & 1), (jt >> 1) & 1, deadline, s_abort, status)))
+        return -1;
+      return s_tidx[jt & 1];
+    };
+
+    // Tile set-up of slot jt (tile t, or the end marker t = -1) into info
     // block jt & 1: this warp's 2 x 32 rows.
-    auto setup = [&](int jt) {
-      const int64_t t = blockIdx.x + static_cast<int64_t>(jt) * gridDim.x;
+    auto setup = [&](int jt, int64_t t) {
       const int ib = jt & 1;
+      if (t < 0) {
+        if (lane == 0) {
+          *reinterpret_cast<int32_t*>(info0 + ib * Info::BYTES + Info::OFF_TILE) = -1;
+          reinterpret_cast<uint32_t*>(info0 + ib * Info::BYTES + Info::OFF_KMASK)[q] = 0u;
+        }
+        tc::mbar_arrive(bar_ifull + 8 * ib);
+        return;
+      }
       int32_t* rows = rows_of(ib);
       int32_t* orow = orow_of(ib);
       uint32_t* lmask = lmask_of(ib);
@@ -369,15 +409,16 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
           act |= (none != kFullMask ? 1u : 0u) << kk;
         }
       }
-      if (lane == 0) reinterpret_cast<uint32_t*>(info0 + ib * Info::BYTES + Info::OFF_KMASK)[q] = act;
+      if (lane == 0) {
+        reinterpret_cast<uint32_t*>(info0 + ib * Info::BYTES + Info::OFF_KMASK)[q] = act;
+        *reinterpret_cast<int32_t*>(info0 + ib * Info::BYTES + Info::OFF_TILE) = static_cast<int32_t>(t);
+      }
       tc::mbar_arrive(bar_ifull + 8 * ib);
     };
 
-    // first two tiles: info blocks 0 and 1 are free
-    const int64_t my_tiles = blockIdx.x < n_tiles ? (n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    for (int jt = 0; jt < 2 && jt < my_tiles; ++jt) setup(jt);
-    // zero both accumulator buffers (MMAs always accumulate) and hand them to
-    // the MMA issuer: arrival #0
+    // zero both accumulator buffers (MMAs always accumulate), set up the first
+    // tile, hand the buffers to the MMA issuer (arrival #0), then set up the
+    // second tile while the first one runs
     for (int b = 0; b < NACC; ++b) {
       __syncwarp();
 #pragma unroll 1
@@ -386,15 +427,20 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
         for (int c0 = 0; c0 < TN; c0 += 32)
           tc::tmem_st32_zero(tmem + (static_cast<uint32_t>(q * 32) << 16) +
                              static_cast<uint32_t>(b * 2 * TN + h * TN + c0));
-      tc::tmem_wait_st();
-      tc::tc_fence_before();
-      tc::mbar_arrive(bar_aempty + 8 * b);
     }
-    int it = 0;
-    for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
+    tc::tmem_wait_st();
+    int64_t tq0 = grab(0);  // tiles of info blocks 0 and 1
+    setup(0, tq0);
+    tc::tc_fence_before();
+    for (int b = 0; b < NACC; ++b) tc::mbar_arrive(bar_aempty + 8 * b);
+    int64_t tq1 = tq0 >= 0 ? grab(1) : -1;
+    if (tq0 >= 0) setup(1, tq1);
+    for (int it = 0;; ++it) {
       const int ib = it & 1;
       const int b = it % NACC;
       const int use = it / NACC;
+      const int64_t t = ib ? tq1 : tq0;
+      if (t < 0) break;
       const int64_t row_tile = t / n_col_tiles;
       const int n0 = static_cast<int>(t - row_tile * n_col_tiles) * TN;
       if (!__all_sync(kFullMask, tc::mbar_wait(bar_afull + 8 * b, use & 1, deadline, s_abort, status))) break;
@@ -456,11 +502,14 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
       tc::mbar_arrive(bar_aempty + 8 * b);
       // prepare the tile two ahead in this info block once the producers and
       // the MMA issuer have released it
-      if (it + 2 < my_tiles) {
-        if (!__all_sync(kFullMask, tc::mbar_wait(bar_iempty + 8 * ib, (it >> 1) & 1, deadline, s_abort, status)))
-          break;
-        setup(it + 2);
-      }
+      if (!__all_sync(kFullMask, tc::mbar_wait(bar_iempty + 8 * ib, (it >> 1) & 1, deadline, s_abort, status)))
+        break;
+      const int64_t tn = grab(it + 2);
+      setup(it + 2, tn);
+      if (ib)
+        tq1 = tn;
+      else
+        tq0 = tn;
     }
   }
 

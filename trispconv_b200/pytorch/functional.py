@@ -120,7 +120,7 @@ def conv_launch(features: torch.Tensor, weight: torch.Tensor, weight_layout: int
                               w.data_ptr(), weight_layout, L.ptr(b), L.ptr(gather), L.ptr(order), k_vol, n_out,
                               c_out, L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(),
                               (L.CONV_RELU if relu else 0) | _FORCE_FLAGS, L.status_word(dev).data_ptr(),
-                              L.stream_ptr(dev))
+                              L.tile_counter(dev).data_ptr(), L.stream_ptr(dev))
     L.check(rc, "tsc_conv_forward")
     if L.EAGER_CHECKS:
         L.check_device_status(dev)
