@@ -227,8 +227,33 @@ def check_device_status(device: Optional[torch.device] = None) -> None:
 EAGER_CHECKS = os.environ.get("TRISPCONV_B200_EAGER_CHECKS", "0") == "1"
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device) -> int:
+    """cudaStream_t of the current stream on `device`."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
+
+
+class _NoSwitch:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NO_SWITCH = _NoSwitch()
+
+
+def on_device(device: torch.device):
+    """torch.cuda.device(device), skipped when it is already current (the
+    library's entry points launch on the current device)."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return _NO_SWITCH
+    return torch.cuda.device(device)
 
 
 def ptr(t: Optional[torch.Tensor]) -> Optional[int]:

@@ -82,7 +82,7 @@ def build_row_order(km: "KernelMap") -> torch.Tensor:
     lib = L.load()
     order = torch.empty(km.n_out, dtype=torch.int32, device=dev)
     ws = L.workspace(lib.tsc_row_order_workspace(km.n_out), dev)
-    with torch.cuda.device(dev):
+    with L.on_device(dev):
         L.check(lib.tsc_row_order(km.gather.data_ptr(), km.k_vol, km.n_out, ws.data_ptr(), ws.numel(),
                                   order.data_ptr(), L.status_word(dev).data_ptr(), L.stream_ptr(dev)),
                 "tsc_row_order")
@@ -118,12 +118,16 @@ class IndiceData:
         self.subm = subm
         self._kmap = kmap
         self._pair_num_from = pair_num_from
+        self._ready = None  # CUDA event: map built on a side stream (kmap_stream)
 
     # -- lazily materialised reference fields -------------------------------
     def _materialize(self) -> None:
         km = self._kmap
         if km is None:
             raise RuntimeError("IndiceData has neither pair lists nor a device kernel map")
+        from trispconv_b200.pytorch.kmap_stream import wait_ready
+
+        wait_ready(self)
         counts = self.pair_num
         K = km.k_vol
         total = int(counts.sum())
@@ -172,6 +176,9 @@ class IndiceData:
             if self._pair_num_from is not None:
                 self._pair_num = self._pair_num_from.pair_num
             else:
+                from trispconv_b200.pytorch.kmap_stream import wait_ready
+
+                wait_ready(self)
                 km = self._kmap
                 meta = km.meta[L.META_COUNTS:L.META_COUNTS + km.k_vol].cpu()
                 L.raise_status(int(L.status_word(km.device).item()), km.device)
@@ -223,7 +230,7 @@ def generate_subm_indice_pairs(indices: torch.Tensor, spatial_shape, batch_size:
     gather = torch.empty((K, n), dtype=torch.int32, device=dev)
     meta = torch.empty(L.META_COUNTS + K, dtype=torch.int64, device=dev)
     ws = L.workspace(lib.tsc_subm_kmap_workspace(n), dev)
-    with torch.cuda.device(dev):
+    with L.on_device(dev):
         L.check(lib.tsc_subm_kmap(idx.data_ptr(), n, L.byref(geo), ws.data_ptr(), ws.numel(),
                                   gather.data_ptr(), meta.data_ptr(), L.status_word(dev).data_ptr(),
                                   L.stream_ptr(dev)), "tsc_subm_kmap")
@@ -264,23 +271,23 @@ def generate_strided_indice_pairs(indices: torch.Tensor, spatial_shape, batch_si
     geo = L.make_geometry(batch_size, shape, out_shape, ks, st, pd, dl)
     ws = L.workspace(lib.tsc_strided_kmap_workspace(L.byref(geo)), dev)
     meta = torch.empty(L.META_COUNTS + K, dtype=torch.int64, device=dev)
+    scatter = torch.empty((K, n_in), dtype=torch.int32, device=dev)  # size known before the count
     status = L.status_word(dev)
     stream = L.stream_ptr(dev)
-    with torch.cuda.device(dev):
+    with L.on_device(dev):
         L.check(lib.tsc_strided_kmap_count(idx.data_ptr(), n_in, L.byref(geo), ws.data_ptr(), ws.numel(),
                                            meta.data_ptr(), status.data_ptr(), stream),
                 "tsc_strided_kmap_count")
-        host = meta.cpu()  # the one synchronisation: output count + status
+        host = meta.cpu().tolist()  # the one synchronisation: output count + status
         L.raise_status(int(host[L.META_STATUS]), dev)
-        n_out = int(host[L.META_N_OUT])
-        n_part = int(host[L.META_N_PART])
-        counts = host[L.META_COUNTS:].clone()
+        n_out = host[L.META_N_OUT]
+        n_part = host[L.META_N_PART]
+        counts = host[L.META_COUNTS:]
         if n_out == 0:
             return _empty_strided(indices, K, shape, out_shape, ks, st, pd, dl)
-        total_pairs = int(counts.sum())
+        total_pairs = sum(counts)
         out_indices = torch.empty((n_out, 4), dtype=torch.int32, device=dev)
         gather = torch.empty((K, n_out), dtype=torch.int32, device=dev)
-        scatter = torch.empty((K, n_in), dtype=torch.int32, device=dev)
         overflow = torch.empty((max(total_pairs, 1), 3), dtype=torch.int32, device=dev)
         L.check(lib.tsc_strided_kmap_emit(idx.data_ptr(), n_in, L.byref(geo), ws.data_ptr(), ws.numel(),
                                           n_out, out_indices.data_ptr(), gather.data_ptr(),
@@ -290,7 +297,7 @@ def generate_strided_indice_pairs(indices: torch.Tensor, spatial_shape, batch_si
     _eager_check(dev)
     km = KernelMap(K, n_in, n_out, gather, meta, dev, scatter=scatter, overflow=overflow,
                    overflow_cap=overflow.shape[0], pair_map=scatter, pair_mode=1, n_part=n_part)
-    return IndiceData(out_indices=out_indices, pair_num=counts.to(torch.long), input_indices=indices,
+    return IndiceData(out_indices=out_indices, pair_num=torch.tensor(counts, dtype=torch.long), input_indices=indices,
                       input_spatial_shape=tuple(spatial_shape), output_spatial_shape=out_shape,
                       kernel_size=ks, stride=st, padding=pd, dilation=dl, subm=False, kmap=km)
 
@@ -322,7 +329,7 @@ def kmap_from_pairs(pairs_in: Sequence[torch.Tensor], pairs_out: Sequence[torch.
     meta = torch.zeros(L.META_COUNTS + K, dtype=torch.int64, device=device)
     overflow = torch.empty((max(total, 1), 3), dtype=torch.int32, device=device)
     lib = L.load()
-    with torch.cuda.device(device):
+    with L.on_device(device):
         L.check(lib.tsc_gather_from_pairs(pin.data_ptr(), pout.data_ptr(), off_arr, K, n_out,
                                           gather.data_ptr(), overflow.data_ptr(), overflow.shape[0],
                                           meta.data_ptr(), L.status_word(device).data_ptr(),
@@ -364,7 +371,7 @@ def inverse_indice_data(fwd: IndiceData) -> Tuple[IndiceData, int]:
             inv_gather = torch.empty((K, n_part), dtype=torch.int32, device=dev)
         if n_in > 0:
             ws = L.workspace(lib.tsc_inverse_kmap_workspace(n_in), dev)
-            with torch.cuda.device(dev):
+            with L.on_device(dev):
                 L.check(lib.tsc_inverse_kmap_strided(in_idx.data_ptr(), n_in, km.scatter.data_ptr(), K, n_part,
                                                      ws.data_ptr(), ws.numel(), out_indices.data_ptr(),
                                                      inv_gather.data_ptr(), None, status.data_ptr(), stream),
@@ -377,7 +384,7 @@ def inverse_indice_data(fwd: IndiceData) -> Tuple[IndiceData, int]:
         compact = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
         meta = torch.empty(L.META_COUNTS + K, dtype=torch.int64, device=dev)
         ws = L.workspace(lib.tsc_inverse_kmap_workspace(n), dev)
-        with torch.cuda.device(dev):
+        with L.on_device(dev):
             L.check(lib.tsc_inverse_kmap_subm_count(km.gather.data_ptr(), K, n, ws.data_ptr(), ws.numel(),
                                                     compact.data_ptr(), meta.data_ptr(), status.data_ptr(),
                                                     stream), "tsc_inverse_kmap_subm_count")

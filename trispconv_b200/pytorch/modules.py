@@ -23,6 +23,7 @@ from trispconv_b200.pytorch.indices import (
     generate_subm_indice_pairs,
     inverse_indice_data,
 )
+from trispconv_b200.pytorch.kmap_stream import KmapScope, wait_ready
 from trispconv_b200.pytorch.tensor import SparseConvTensor
 from trispconv_b200.pytorch.weight import normalize_spconv_weight
 
@@ -90,6 +91,7 @@ class SparseConvolution(SparseModule):
         if features.shape[1] != self.in_channels:
             raise RuntimeError(f"features have {features.shape[1]} channels, "
                                f"{type(self).__name__} expects {self.in_channels}")
+        wait_ready(data)
         km = None
         if data is not None and n_out > 0:
             km = kernel_map_for(data, n_out, features.device)
@@ -114,8 +116,10 @@ class SparseConvolution(SparseModule):
     def _get_or_compute_subm_indice(self, x: SparseConvTensor) -> IndiceData:
         if self.indice_key is not None and self.indice_key in x.indice_dict:
             return x.indice_dict[self.indice_key]
-        data = generate_subm_indice_pairs(x.indices, tuple(x.spatial_shape), x.batch_size,
-                                          self.kernel_size, self.dilation)
+        with KmapScope(x.indices) as scope:
+            data = generate_subm_indice_pairs(x.indices, tuple(x.spatial_shape), x.batch_size,
+                                              self.kernel_size, self.dilation)
+        scope.finish(data)
         if self.indice_key is not None:
             x.indice_dict[self.indice_key] = data
         return data
@@ -123,8 +127,10 @@ class SparseConvolution(SparseModule):
     def _get_or_compute_strided_indice(self, x: SparseConvTensor) -> IndiceData:
         if self.indice_key is not None and self.indice_key in x.indice_dict:
             return x.indice_dict[self.indice_key]
-        data = generate_strided_indice_pairs(x.indices, tuple(x.spatial_shape), x.batch_size,
-                                             self.kernel_size, self.stride, self.padding, self.dilation)
+        with KmapScope(x.indices) as scope:
+            data = generate_strided_indice_pairs(x.indices, tuple(x.spatial_shape), x.batch_size,
+                                                 self.kernel_size, self.stride, self.padding, self.dilation)
+        scope.finish(data)
         if self.indice_key is not None:
             x.indice_dict[self.indice_key] = data
         return data
@@ -160,7 +166,10 @@ class SparseConvolution(SparseModule):
                                     indice_dict=x.indice_dict)
         inv = getattr(fwd, "_inverse_cache", None)
         if inv is None:
-            inv = inverse_indice_data(fwd)
+            with KmapScope(fwd.out_indices) as scope:
+                wait_ready(fwd)
+                inv = inverse_indice_data(fwd)
+            scope.finish(inv[0])
             fwd._inverse_cache = inv
         data, n_out = inv
         out = self._conv(x.features, data, n_out, relu)

@@ -94,7 +94,7 @@ def _dense_cuda(feats: torch.Tensor, indices: torch.Tensor, B: int, C: int, shap
     shape_arr = (L.c_int32 * 3)(*shape)
     status = L.status_word(dev)
     lib = L.load()
-    with torch.cuda.device(dev):
+    with L.on_device(dev):
         L.check(lib.tsc_to_dense(f.data_ptr() if f.numel() else None, L.DTYPE_CODE[feats.dtype],
                                  idx.data_ptr() if idx.numel() else None, idx.shape[0], C, B, shape_arr,
                                  1 if channels_first else 0, out.data_ptr(), status.data_ptr(),
