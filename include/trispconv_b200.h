@@ -70,6 +70,7 @@ extern "C" {
 #define TSC_CONV_FORCE_SIMT 0x100  /* testing: use the CUDA-core kernel even when a tensor-core one applies */
 #define TSC_CONV_USE_TC     0x200  /* use the tcgen05 (TMEM) kernel where it applies */
 #define TSC_CONV_TC_SIMPLE  0x400  /* testing: one-tile-per-CTA tcgen05 kernel instead of the persistent one */
+#define TSC_CONV_NO_RESIDENT_W 0x800  /* testing: mma.sync kernel without resident weights */
 
 /* Weight layouts accepted by tsc_conv_forward. */
 #define TSC_W_KCC  0  /* (K, C_in, C_out): the reference's internal layout (weight.py:36) */

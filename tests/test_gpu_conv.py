@@ -307,3 +307,34 @@ def test_tensor_core_matches_cuda_core_kernel(cuda, dtype, cin, cout, ks):
         err = (a.features.float() - b.features.float()).abs().max().item()
         ulp = 2 ** -7 if dtype == torch.bfloat16 else 2 ** -10
         assert err <= 2 * ulp * max(scale, 1e-3), (kind, err, scale)
+
+
+@pytest.mark.parametrize("cin,cout", [(4, 16), (16, 16), (16, 32), (32, 32), (32, 64), (8, 24)])
+def test_mma_resident_weights_match_streamed_weights(cuda, cin, cout):
+    """The persistent mma.sync kernel with resident weights gives the same
+    bits as the kernel that streams the weights per tile."""
+    from trispconv_b200 import _lib as L
+    from trispconv_b200.pytorch.indices import generate_subm_indice_pairs
+
+    rng = np.random.default_rng(cin * 100 + cout)
+    shape = (40, 80, 80)
+    n = 60_000
+    cells = rng.choice(int(np.prod(shape)), n, replace=False)
+    z, y, x = np.unravel_index(cells, shape)
+    idx = torch.from_numpy(np.stack([np.zeros(n), z, y, x], 1).astype(np.int32)).to(cuda)
+    km = generate_subm_indice_pairs(idx, shape, 1, 3)._kmap
+    f = torch.from_numpy(rng.standard_normal((n, cin)).astype(np.float32)).to(cuda).half()
+    w = (torch.randn(cout, 3, 3, 3, cin, device=cuda) * 0.1).half()
+    b = torch.randn(cout, device=cuda).half()
+    outs = []
+    for extra in (0, L.CONV_NO_RESIDENT_W):
+        out = torch.empty(n, cout, dtype=torch.half, device=cuda)
+        rc = L.load().tsc_conv_forward(f.data_ptr(), L.DTYPE_CODE[torch.float16], n, cin, w.data_ptr(), L.W_KRSC,
+                                       b.data_ptr(), km.gather.data_ptr(), None, 27, n, cout, None, 0,
+                                       km.meta.data_ptr(), out.data_ptr(), L.CONV_RELU | extra,
+                                       L.status_word(cuda).data_ptr(), None, L.stream_ptr(cuda))
+        L.check(rc, "tsc_conv_forward")
+        outs.append(out)
+    torch.cuda.synchronize()
+    L.check_device_status(cuda)
+    assert torch.equal(outs[0], outs[1])

@@ -40,6 +40,7 @@ CONV_RELU = 0x1
 CONV_FORCE_SIMT = 0x100
 CONV_USE_TC = 0x200
 CONV_TC_SIMPLE = 0x400
+CONV_NO_RESIDENT_W = 0x800
 
 W_KCC = 0   # (K, C_in, C_out)
 W_KRSC = 1  # (C_out, kD, kH, kW, C_in)

@@ -20,10 +20,47 @@ static_assert(mma::KMAX == kMmaKMax && tc::KMAX == kMmaKMax, "kernel K limits");
 
 // ---- tensor-core (mma.sync) path -------------------------------------------
 
+// Persistent mma.sync kernel with the column tile's weights resident in
+// shared memory (one channel chunk, weights <= mma::kMaxResidentWeightBytes).
+template <typename T, int TN, int KC, int CH>
+int launch_mmaw_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
+                    const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
+                    const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+  using C = mma::CfgW<TN, KC>;
+  auto kern = mma::k_conv_mmaw<T, TN, KC, CH>;
+  constexpr int kMaxSmem = C::MAIN + mma::kMaxResidentWeightBytes + (mma::KMAX * mma::BM + mma::BM + mma::KMAX + 8) * 4;
+  static unsigned long long configured = 0;
+  static int ctas_per_sm[mma::KMAX + 1][64] = {};  // [K][device]: 0 = not computed yet
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 63;
+  if (!(configured & (1ull << dev))) {
+    TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+    configured |= 1ull << dev;
+  }
+  const int smem = C::bytes(K);
+  int& occ = ctas_per_sm[K][dev];
+  if (occ == 0) {
+    TSC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, mma::NT, smem));
+    if (occ < 1) occ = 1;
+  }
+  const int64_t row_tiles = ceil_div(n_out, mma::BM);
+  const int64_t cap = static_cast<int64_t>(sm_count()) * occ;
+  dim3 grid(static_cast<unsigned>(row_tiles < cap ? row_tiles : cap), static_cast<unsigned>(ceil_div(c_out, TN)));
+  kern<<<grid, mma::NT, smem, stream>>>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
+                                        flags, status);
+  TSC_LAUNCH_CHECK("k_conv_mmaw");
+  return TSC_OK;
+}
+
 template <typename T, int TN, int KC, int CH>
 int launch_mma_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                    const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
                    const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+  if ((flags & TSC_CONV_NO_RESIDENT_W) == 0 && c_in <= KC && K <= mma::KMAX &&
+      static_cast<int64_t>(K) * TN * KC * 2 <= mma::kMaxResidentWeightBytes)
+    return launch_mmaw_cfg<T, TN, KC, CH>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
+                                          out, flags, status, stream);
   using C = mma::Cfg<TN, KC>;
   auto kern = mma::k_conv_mma<T, TN, KC, CH>;
   static unsigned long long configured = 0;  // one bit per device

@@ -302,5 +302,243 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent variant with resident weights (layers whose whole weight slice
+// of one column tile fits in shared memory: C_in <= KC, one channel chunk).
+// Each CTA loads W[n0:n0+TN, :, :] once, in the swizzled B-tile layout, and
+// then walks row tiles; the ring carries only the gathered feature rows.
+// Compared with k_conv_mma this removes the per-tile weight reload and the
+// per-CTA launch cost; it pays off only for small weight blocks (below).
+// ---------------------------------------------------------------------------
+
+template <int TN, int KC>
+struct CfgW {
+  static constexpr int A_BYTES = BM * KC * 2;
+  static constexpr int PIPE = NS * A_BYTES;
+  static constexpr int OUT_LD = TN + 8;
+  static constexpr int EPI = BM * OUT_LD * 4;
+  static constexpr int MAIN = PIPE > EPI ? PIPE : EPI;
+  static constexpr int WSLICE = TN * KC * 2;  // one offset's B tile
+  static constexpr int bytes(int K) { return MAIN + K * WSLICE + (K * BM + BM + KMAX + 8) * 4; }
+};
+
+// Largest resident weight block taken.  Measured on the config-3 maps: 16->16
+// (14 KB) is 15 % faster resident, 16->32 (28 KB) breaks even, and 32->32
+// (55 KB) and 32->64 (111 KB) are slower, because the larger shared-memory
+// footprint halves the CTAs per SM that hide the gather latency.
+constexpr int kMaxResidentWeightBytes = 16 * 1024;
+
+template <typename T, int TN, int KC, int CH>
+__global__ void __launch_bounds__(NT)
+k_conv_mmaw(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__ W,
+            const T* __restrict__ bias, const int32_t* __restrict__ gmap, const int32_t* __restrict__ perm,
+            int K, int64_t n_out, int c_out, const int32_t* __restrict__ ovf, int64_t ovf_cap,
+            const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status) {
+  using C = CfgW<TN, KC>;
+  constexpr int WN = (TN == 128) ? 2 : 1;
+  constexpr int WM = 8 / WN;
+  constexpr int WTM = BM / WM;
+  constexpr int WTN = TN / WN;
+  constexpr int MF = WTM / 16;
+  constexpr int NF = WTN / 8;
+  constexpr int UPR = KC * 2 / CH;  // copy units per shared-memory row
+  static_assert(NF % 2 == 0, "B fragments are loaded in pairs");
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  unsigned char* s_w = smem + C::MAIN;                                             // [K][TN][KC]
+  int32_t* s_rows = reinterpret_cast<int32_t*>(s_w + static_cast<int64_t>(K) * C::WSLICE);  // [K][BM]
+  int32_t* s_orow = s_rows + K * BM;
+  int32_t* s_klist = s_orow + BM;
+  int32_t* s_misc = s_klist + KMAX;
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int n0 = blockIdx.y * TN;
+  const int64_t n_row_tiles = (n_out + BM - 1) / BM;
+  const bool relu = (flags & TSC_CONV_RELU) != 0;
+
+  // ---- resident weights: W[n0 + nn, k, 0:c_in] for all k --------------------
+  for (int u = tid; u < K * TN * UPR; u += NT) {
+    const int k = u / (TN * UPR);
+    const int rem = u - k * (TN * UPR);
+    const int nn = rem / UPR;
+    const int q = rem - nn * UPR;
+    const int c = q * (CH / 2);
+    const int n = n0 + nn;
+    const bool valid = n < c_out && c < c_in;
+    const int byte = q * CH;
+    unsigned char* dst = s_w + k * C::WSLICE + nn * (KC * 2) + (swz<KC>(nn, byte >> 4) << 4) + (byte & 15);
+    const T* src = valid ? W + (static_cast<int64_t>(n) * K + k) * c_in + c : W;
+    cp_async<CH>(dst, src, valid);
+  }
+  cp_commit();
+
+  const int wm = warp / WN;
+  const int wn = warp % WN;
+
+  for (int64_t tile = blockIdx.x; tile < n_row_tiles; tile += gridDim.x) {
+    const int64_t tile0 = tile * BM;
+    // ---- the tile's output rows and gather-map slice -------------------------
+    if (tid < KMAX) s_klist[tid] = 0;
+    if (tid < BM) {
+      const int64_t t = tile0 + tid;
+      s_orow[tid] = t < n_out ? (perm != nullptr ? __ldg(&perm[t]) : static_cast<int32_t>(t)) : -1;
+    }
+    __syncthreads();
+    for (int e = tid; e < K * BM; e += NT) {
+      const int k = e / BM;
+      const int r = e - k * BM;
+      const int o = s_orow[r];
+      int j = -1;
+      if (o >= 0) {
+        j = gmap != nullptr ? __ldg(&gmap[static_cast<int64_t>(k) * n_out + o]) : o;
+        if (j >= n_in) {
+          raise_status(status, TSC_STATUS_KEY_RANGE);
+          j = -1;
+        }
+      }
+      s_rows[e] = j;
+      if (j >= 0) s_klist[k] = 1;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int na = 0;
+      for (int k = 0; k < K; ++k)
+        if (s_klist[k]) s_klist[na++] = k;
+      s_misc[0] = na;
+    }
+    __syncthreads();
+    const int steps = s_misc[0];
+
+    auto load_stage = [&](int s, int buf) {
+      const int k = s_klist[s];
+      unsigned char* sa = smem + buf * C::A_BYTES;
+      for (int u = tid; u < BM * UPR; u += NT) {
+        const int r = u / UPR;
+        const int q = u - r * UPR;
+        const int c = q * (CH / 2);
+        const int j = s_rows[k * BM + r];
+        const bool valid = j >= 0 && c < c_in;
+        const int byte = q * CH;
+        unsigned char* dst = sa + r * (KC * 2) + (swz<KC>(r, byte >> 4) << 4) + (byte & 15);
+        const T* src = valid ? F + static_cast<int64_t>(j) * c_in + c : F;
+        cp_async<CH>(dst, src, valid);
+      }
+    };
+
+    float acc[MF][NF][4];
+#pragma unroll
+    for (int a = 0; a < MF; ++a)
+#pragma unroll
+      for (int b = 0; b < NF; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
+
+#pragma unroll
+    for (int s = 0; s < NS - 1; ++s) {
+      if (s < steps) load_stage(s, s);
+      cp_commit();
+    }
+    for (int s = 0; s < steps; ++s) {
+      cp_wait<NS - 2>();
+      __syncthreads();
+      const int nxt = s + NS - 1;
+      if (nxt < steps) load_stage(nxt, nxt % NS);
+      cp_commit();
+      const unsigned char* sa = smem + (s % NS) * C::A_BYTES;
+      const unsigned char* sb = s_w + s_klist[s] * C::WSLICE;
+#pragma unroll
+      for (int kk = 0; kk < KC / 16; ++kk) {
+        uint32_t af[MF][4];
+#pragma unroll
+        for (int mf = 0; mf < MF; ++mf) {
+          const int row = wm * WTM + mf * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int chunk = kk * 2 + (lane >> 4);
+          ldsm_x4(af[mf], smem_u32(sa + row * (KC * 2) + (swz<KC>(row, chunk) << 4)));
+        }
+#pragma unroll
+        for (int nf2 = 0; nf2 < NF / 2; ++nf2) {
+          uint32_t bf[4];
+          const int g = lane >> 3;
+          const int row = wn * WTN + nf2 * 16 + (g >> 1) * 8 + (lane & 7);
+          const int chunk = kk * 2 + (g & 1);
+          ldsm_x4(bf, smem_u32(sb + row * (KC * 2) + (swz<KC>(row, chunk) << 4)));
+#pragma unroll
+          for (int mf = 0; mf < MF; ++mf) {
+            mma16816<T>(acc[mf][2 * nf2], af[mf], bf[0], bf[1]);
+            mma16816<T>(acc[mf][2 * nf2 + 1], af[mf], bf[2], bf[3]);
+          }
+        }
+      }
+    }
+    cp_wait<0>();
+    __syncthreads();
+
+    // ---- epilogue: fp32 tile in shared memory (over the ring) --------------
+    float* s_out = reinterpret_cast<float*>(smem);
+#pragma unroll
+    for (int mf = 0; mf < MF; ++mf) {
+#pragma unroll
+      for (int nf = 0; nf < NF; ++nf) {
+        const int row = wm * WTM + mf * 16 + (lane >> 2);
+        const int col = wn * WTN + nf * 8 + (lane & 3) * 2;
+        *reinterpret_cast<float2*>(&s_out[row * C::OUT_LD + col]) = make_float2(acc[mf][nf][0], acc[mf][nf][1]);
+        *reinterpret_cast<float2*>(&s_out[(row + 8) * C::OUT_LD + col]) =
+            make_float2(acc[mf][nf][2], acc[mf][nf][3]);
+      }
+    }
+    __syncthreads();
+
+    // Pairs that did not fit the gather map (duplicate input coordinates).
+    if (ovf != nullptr && meta != nullptr) {
+      int64_t n_ovf = static_cast<int64_t>(__ldg(&meta[TSC_META_N_OVERFLOW]));
+      if (n_ovf > ovf_cap) n_ovf = ovf_cap;
+      for (int64_t e = 0; e < n_ovf; ++e) {
+        const int k = __ldg(&ovf[3 * e + 0]);
+        const int o = __ldg(&ovf[3 * e + 1]);
+        const int j = __ldg(&ovf[3 * e + 2]);
+        if (tid == 0) s_misc[1] = -1;
+        __syncthreads();
+        if (tid < BM && s_orow[tid] == o) s_misc[1] = tid;
+        __syncthreads();
+        const int r = s_misc[1];
+        if (r >= 0 && k >= 0 && k < K && j >= 0 && j < n_in && tid < TN && n0 + tid < c_out) {
+          const T* wrow = W + (static_cast<int64_t>(n0 + tid) * K + k) * c_in;
+          const T* frow = F + static_cast<int64_t>(j) * c_in;
+          float sacc = 0.f;
+          for (int c = 0; c < c_in; ++c) sacc = fmaf(to_f32(frow[c]), to_f32(wrow[c]), sacc);
+          s_out[r * C::OUT_LD + tid] += sacc;
+        }
+        __syncthreads();
+      }
+    }
+
+    constexpr int CPR_OUT = TN / 8;  // 16-byte output chunks per row
+    for (int u = tid; u < BM * CPR_OUT; u += NT) {
+      const int r = u / CPR_OUT;
+      const int q = u - r * CPR_OUT;
+      const int o = s_orow[r];
+      const int n = n0 + q * 8;
+      if (o < 0 || n >= c_out) continue;
+      const float* src = &s_out[r * C::OUT_LD + q * 8];
+      union {
+        uint4 v;
+        T h[8];
+      } pk;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float v = src[i];
+        if (bias != nullptr) v += to_f32(bias[n + i]);
+        if (relu) v = fmaxf(v, 0.f);
+        pk.h[i] = from_f32<T>(v);
+      }
+      *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o) * c_out + n) = pk.v;
+    }
+    __syncthreads();  // s_out, s_orow and s_rows are rewritten by the next tile
+  }
+  cp_wait<0>();
+}
+
 }  // namespace mma
 }  // namespace tsc
