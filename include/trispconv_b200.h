@@ -226,6 +226,40 @@ TSC_API int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, 
                      const int32_t* overflow, int64_t overflow_cap, const int64_t* meta,
                      void* out, int32_t flags, int64_t* status, uint32_t* tile_counter, void* stream);
 
+/* ---- per-tile input halos for the convolution ------------------------------
+ * No counterpart in the reference (its CPU path has no tiles): a faster
+ * variant of tsc_conv_forward for 16-bit layers with exactly 64 input
+ * channels.  The persistent tcgen05 kernel computes tiles of
+ * TSC_HALO_TILE_ROWS consecutive output rows; a tile's halo is the list of
+ * distinct input rows its pairs read.  tsc_tile_halo lists them once per map
+ * so that the convolution loads each distinct input row of a tile once into
+ * shared memory instead of once per pair.  Results are identical with and
+ * without a halo.
+ *   tsc_conv_halo_capacity: halo rows per tile the halo kernel holds for this
+ *     layer (dtype, c_in, c_out, K, conv flags), or 0 when it does not apply.
+ *   tsc_tile_halo: from a k-major gather map [k_vol][n_out] (1 <= K <= 27)
+ *     writes, per tile t = o / TSC_HALO_TILE_ROWS, halo_rows[t][capacity]
+ *     (16-byte aligned; the first halo_count[t] entries, padded to a multiple
+ *     of 4 with copies of the last one) and halo_map [k_vol][n_out] int16:
+ *     the position of gather_map[k][o] in its tile's list, -1 for no pair, -2
+ *     for a row beyond the capacity (read from the gather map instead).
+ *   tsc_conv_forward_halo: tsc_conv_forward plus the three halo buffers built
+ *     with `halo_capacity` == tsc_conv_halo_capacity of the layer.  Layers
+ *     the halo kernel does not take (or a row_order) run as in
+ *     tsc_conv_forward. */
+#define TSC_HALO_TILE_ROWS 256
+TSC_API int32_t tsc_conv_halo_capacity(int32_t dtype, int32_t c_in, int32_t c_out, int32_t k_vol, int32_t flags);
+TSC_API int tsc_tile_halo(const int32_t* gather_map, int32_t k_vol, int64_t n_in, int64_t n_out, int32_t capacity,
+                  int32_t* halo_rows, int32_t* halo_count, int16_t* halo_map, int64_t* status, void* stream);
+TSC_API int tsc_conv_forward_halo(const void* features, int32_t dtype, int64_t n_in, int32_t c_in,
+                     const void* weight, int32_t weight_layout, const void* bias,
+                     const int32_t* gather_map, const int32_t* row_order,
+                     int32_t k_vol, int64_t n_out, int32_t c_out,
+                     const int32_t* overflow, int64_t overflow_cap, const int64_t* meta,
+                     void* out, int32_t flags, int64_t* status, uint32_t* tile_counter,
+                     const int32_t* halo_rows, const int32_t* halo_count, const int16_t* halo_map,
+                     int32_t halo_capacity, void* stream);
+
 /* ---- dense scatter ---------------------------------------------------------
  * SparseConvTensor.dense() (tensor.py:72-99): writes features into a zeroed
  * (B, C, D, H, W) (channels_first = 1) or (B, D, H, W, C) tensor.  Rows with

@@ -226,40 +226,42 @@ size_t dtype_size(int dtype) {
 
 using namespace tsc;
 
-extern "C" {
+namespace {
 
-int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t c_in, const void* weight,
-                     int32_t weight_layout, const void* bias, const int32_t* gather_map, const int32_t* row_order, int32_t k_vol, int64_t n_out,
-                     int32_t c_out, const int32_t* overflow, int64_t overflow_cap, const int64_t* meta,
-                     void* out, int32_t flags, int64_t* status, uint32_t* tile_counter, void* stream_) {
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+// Argument checks and kernel choice shared by tsc_conv_forward and
+// tsc_conv_forward_halo.
+int conv_forward(const ConvArgs& a, int32_t dtype, int32_t weight_layout) {
+  const int64_t n_in = a.n_in, n_out = a.n_out;
+  const int c_in = a.c_in, c_out = a.c_out, k_vol = a.k_vol, flags = a.flags;
   TSC_CHECK_ARG(c_in > 0 && c_out > 0, "channel counts must be positive (c_in=%d, c_out=%d)", c_in, c_out);
   TSC_CHECK_ARG(k_vol > 0 && k_vol <= 4096, "kernel volume %d out of range", k_vol);
   TSC_CHECK_ARG(n_in >= 0 && n_in <= 0x7fffffffLL && n_out >= 0 && n_out <= 0x7fffffffLL,
                 "row counts out of range");
-  TSC_CHECK_ARG(status != nullptr, "status is NULL");
-  TSC_CHECK_ARG(gather_map != nullptr || (k_vol == 1 && n_in == n_out),
+  TSC_CHECK_ARG(a.status != nullptr, "status is NULL");
+  TSC_CHECK_ARG(a.gather_map != nullptr || (k_vol == 1 && n_in == n_out),
                 "identity map requires K == 1 and n_in == n_out");
   if (n_out == 0) return TSC_OK;
-  TSC_CHECK_ARG(out != nullptr && weight != nullptr, "NULL buffer");
-  TSC_CHECK_ARG(n_in == 0 || features != nullptr, "features is NULL");
-  TSC_CHECK_ARG(aligned(weight, 16) && aligned(out, 16) && (features == nullptr || aligned(features, 16)),
+  TSC_CHECK_ARG(a.out != nullptr && a.weight != nullptr, "NULL buffer");
+  TSC_CHECK_ARG(n_in == 0 || a.features != nullptr, "features is NULL");
+  TSC_CHECK_ARG(aligned(a.weight, 16) && aligned(a.out, 16) && (a.features == nullptr || aligned(a.features, 16)),
                 "features/weight/out must be 16-byte aligned");
   TSC_CHECK_ARG(weight_layout == TSC_W_KCC || weight_layout == TSC_W_KRSC, "bad weight layout %d",
                 weight_layout);
-  TSC_CHECK_ARG(bias == nullptr || aligned(bias, 4), "bias must be 4-byte aligned");
-  TSC_CHECK_ARG(overflow == nullptr || (meta != nullptr && overflow_cap >= 0),
+  TSC_CHECK_ARG(a.bias == nullptr || aligned(a.bias, 4), "bias must be 4-byte aligned");
+  TSC_CHECK_ARG(a.overflow == nullptr || (a.meta != nullptr && a.overflow_cap >= 0),
                 "overflow list needs its meta buffer");
   const int w_krsc = weight_layout == TSC_W_KRSC;
   const bool force_simt = (flags & TSC_CONV_FORCE_SIMT) != 0;
-  const ConvArgs a{features, n_in, c_in, weight, bias, gather_map, row_order, k_vol, n_out, c_out,
-                   overflow, overflow_cap, meta, out, flags, status, tile_counter, stream};
   const bool f16 = dtype == TSC_F16;
   if (!force_simt && (flags & TSC_CONV_USE_TC) != 0) {
     // the one-tile-per-CTA kernel only on request (testing); otherwise the
-    // persistent kernel where its tile shapes apply, else mma.sync below
+    // persistent kernels where their tile shapes apply, else mma.sync below
     if ((flags & TSC_CONV_TC_SIMPLE) != 0 && tc_eligible(dtype, w_krsc, c_in, c_out, k_vol))
       return f16 ? launch_tc_f16(a) : launch_tc_bf16(a);
+    if (n_in > 0 && (flags & TSC_CONV_TC_SIMPLE) == 0 && a.halo_map != nullptr && a.gather_map != nullptr &&
+        a.row_order == nullptr && tch_eligible(dtype, w_krsc, c_in, c_out, k_vol) &&
+        a.halo_capacity == tch_capacity(c_out))
+      return f16 ? launch_tch_f16(a) : launch_tch_bf16(a);
     if (n_in > 0 && tcp_eligible(dtype, w_krsc, c_in, c_out, k_vol) && (flags & TSC_CONV_TC_SIMPLE) == 0)
       return f16 ? launch_tcp_f16(a) : launch_tcp_bf16(a);
   }
@@ -269,18 +271,57 @@ int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t 
   // the row order, so it is ignored here
   switch (dtype) {
     case TSC_F32:
-      return launch_simt<float>(features, n_in, c_in, weight, weight_layout == TSC_W_KRSC, bias, gather_map, k_vol, n_out, c_out, overflow,
-                                overflow_cap, meta, out, flags, status, stream);
+      return launch_simt<float>(a.features, n_in, c_in, a.weight, w_krsc, a.bias, a.gather_map, k_vol, n_out, c_out,
+                                a.overflow, a.overflow_cap, a.meta, a.out, flags, a.status, a.stream);
     case TSC_F16:
-      return launch_simt<__half>(features, n_in, c_in, weight, weight_layout == TSC_W_KRSC, bias, gather_map, k_vol, n_out, c_out, overflow,
-                                 overflow_cap, meta, out, flags, status, stream);
+      return launch_simt<__half>(a.features, n_in, c_in, a.weight, w_krsc, a.bias, a.gather_map, k_vol, n_out, c_out,
+                                 a.overflow, a.overflow_cap, a.meta, a.out, flags, a.status, a.stream);
     case TSC_BF16:
-      return launch_simt<__nv_bfloat16>(features, n_in, c_in, weight, weight_layout == TSC_W_KRSC, bias, gather_map, k_vol, n_out, c_out,
-                                        overflow, overflow_cap, meta, out, flags, status, stream);
+      return launch_simt<__nv_bfloat16>(a.features, n_in, c_in, a.weight, w_krsc, a.bias, a.gather_map, k_vol, n_out,
+                                        c_out, a.overflow, a.overflow_cap, a.meta, a.out, flags, a.status, a.stream);
     default:
       set_error("unsupported dtype code %d for the convolution", dtype);
       return TSC_ERR_UNSUPPORTED;
   }
+}
+
+}  // namespace
+
+extern "C" {
+
+int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t c_in, const void* weight,
+                     int32_t weight_layout, const void* bias, const int32_t* gather_map, const int32_t* row_order,
+                     int32_t k_vol, int64_t n_out, int32_t c_out, const int32_t* overflow, int64_t overflow_cap,
+                     const int64_t* meta, void* out, int32_t flags, int64_t* status, uint32_t* tile_counter,
+                     void* stream) {
+  const ConvArgs a{features, n_in,     c_in,  weight, bias,   gather_map,   row_order,
+                   k_vol,    n_out,    c_out, overflow, overflow_cap, meta, out,
+                   flags,    status,   tile_counter, static_cast<cudaStream_t>(stream)};
+  return conv_forward(a, dtype, weight_layout);
+}
+
+int tsc_conv_forward_halo(const void* features, int32_t dtype, int64_t n_in, int32_t c_in, const void* weight,
+                          int32_t weight_layout, const void* bias, const int32_t* gather_map,
+                          const int32_t* row_order, int32_t k_vol, int64_t n_out, int32_t c_out,
+                          const int32_t* overflow, int64_t overflow_cap, const int64_t* meta, void* out,
+                          int32_t flags, int64_t* status, uint32_t* tile_counter, const int32_t* halo_rows,
+                          const int32_t* halo_count, const int16_t* halo_map, int32_t halo_capacity, void* stream) {
+  TSC_CHECK_ARG(halo_map == nullptr || (halo_rows != nullptr && halo_count != nullptr && aligned(halo_rows, 16)),
+                "halo_map needs halo_rows (16-byte aligned) and halo_count");
+  ConvArgs a{features, n_in,     c_in,  weight, bias,   gather_map,   row_order,
+             k_vol,    n_out,    c_out, overflow, overflow_cap, meta, out,
+             flags,    status,   tile_counter, static_cast<cudaStream_t>(stream)};
+  a.halo_rows = halo_rows;
+  a.halo_count = halo_count;
+  a.halo_map = halo_map;
+  a.halo_capacity = halo_capacity;
+  return conv_forward(a, dtype, weight_layout);
+}
+
+int32_t tsc_conv_halo_capacity(int32_t dtype, int32_t c_in, int32_t c_out, int32_t k_vol, int32_t flags) {
+  if ((flags & TSC_CONV_USE_TC) == 0 || (flags & (TSC_CONV_TC_SIMPLE | TSC_CONV_FORCE_SIMT)) != 0) return 0;
+  if (!tch_eligible(dtype, 1, c_in, c_out, k_vol)) return 0;
+  return tch_capacity(c_out);
 }
 
 int tsc_to_dense(const void* features, int32_t dtype, const int32_t* indices, int64_t n, int32_t c,

@@ -29,6 +29,11 @@ struct ConvArgs {
   int64_t* status;
   uint32_t* tile_counter;  // persistent kernel: dynamic tile hand-out (NULL = round robin)
   cudaStream_t stream;
+  // per-tile input halos (tsc_tile_halo); NULL = none
+  const int32_t* halo_rows = nullptr;
+  const int32_t* halo_count = nullptr;
+  const int16_t* halo_map = nullptr;
+  int halo_capacity = 0;
 };
 
 // Largest kernel volumes the tensor-core kernels take (gather-map slice in
@@ -63,11 +68,23 @@ inline bool tcp_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
   return tc_eligible(dtype, w_krsc, c_in, c_out, K) && c_in % 64 == 0 && c_out % 32 == 0 && K <= kPersistentKMax;
 }
 
+// halo kernel (persistent tcgen05, tile inputs staged once in shared
+// memory): the persistent kernel's shapes with exactly 64 input channels.
+inline bool tch_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
+  return tcp_eligible(dtype, w_krsc, c_in, c_out, K) && c_in == 64;
+}
+
+// Halo rows per tile the halo kernel holds in shared memory for c_out
+// output channels (depends on the tile width it picks).
+int tch_capacity(int c_out);
+
 int launch_mma_f16(const ConvArgs& a);
 int launch_mma_bf16(const ConvArgs& a);
 int launch_tc_f16(const ConvArgs& a);
 int launch_tc_bf16(const ConvArgs& a);
 int launch_tcp_f16(const ConvArgs& a);
 int launch_tcp_bf16(const ConvArgs& a);
+int launch_tch_f16(const ConvArgs& a);
+int launch_tch_bf16(const ConvArgs& a);
 
 }  // namespace tsc

@@ -9,6 +9,7 @@
 #include "conv_launch.h"
 #include "conv_mma.cuh"
 #include "conv_tc.cuh"
+#include "conv_tch.cuh"
 #include "conv_tcp.cuh"
 #include "tsc_common.cuh"
 
@@ -246,6 +247,59 @@ int launch_tcp(const void* F, int64_t n_in, int c_in, const void* W, const void*
                                  status, tile_counter, stream);
 }
 
+
+// ---- persistent tcgen05 path with per-tile halos (C_in == 64) --------------------
+
+template <typename T, int TN>
+int launch_tch_tn(const ConvArgs& a) {
+  using C = tch::Cfg<TN>;
+  auto kern = tch::k_conv_tch<T, TN>;
+  const T* f = static_cast<const T*>(a.features);
+  const T* w = static_cast<const T*>(a.weight);
+  CUtensorMap mf, mw;
+  int rc = encode_maps<T, TN, tch::KC>(f, a.n_in, a.c_in, w, a.k_vol, a.c_out, &mf, &mw);
+  if (rc != TSC_OK) return rc;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL));
+    configured |= 1ull << (dev & 63);
+  }
+  const int64_t tiles = ceil_div(a.n_out, tch::BMT) * ceil_div(a.c_out, TN);
+  const int64_t grid = tiles < sm_count() ? tiles : sm_count();
+  if (a.tile_counter != nullptr) TSC_CUDA(cudaMemsetAsync(a.tile_counter, 0, sizeof(uint32_t), a.stream));
+  kern<<<static_cast<unsigned>(grid), tch::NT, C::TOTAL, a.stream>>>(
+      mf, mw, f, a.n_in, w, static_cast<const T*>(a.bias), a.gather_map, a.k_vol, a.n_out, a.c_out, a.overflow,
+      a.overflow_cap, a.meta, static_cast<T*>(a.out), a.flags, a.status, a.tile_counter, a.halo_rows, a.halo_count,
+      a.halo_map);
+  TSC_LAUNCH_CHECK("k_conv_tch");
+  return TSC_OK;
+}
+
+// Tile width of the halo kernel: the largest UMMA N that divides c_out.
+inline int tch_tile_width(int c_out) {
+  return c_out % 256 == 0 ? 256 : (c_out % 128 == 0 ? 128 : (c_out % 64 == 0 ? 64 : 32));
+}
+
+inline int tch_capacity_of(int c_out) {
+  switch (tch_tile_width(c_out)) {
+    case 256: return tch::Cfg<256>::HALO;
+    case 128: return tch::Cfg<128>::HALO;
+    case 64: return tch::Cfg<64>::HALO;
+    default: return tch::Cfg<32>::HALO;
+  }
+}
+
+template <typename T>
+int launch_tch(const ConvArgs& a) {
+  switch (tch_tile_width(a.c_out)) {
+    case 256: return launch_tch_tn<T, 256>(a);
+    case 128: return launch_tch_tn<T, 128>(a);
+    case 64: return launch_tch_tn<T, 64>(a);
+    default: return launch_tch_tn<T, 32>(a);
+  }
+}
 
 template <typename T>
 int launch_tc(const void* F, int64_t n_in, int c_in, const void* W, const void* bias, const int32_t* gmap,

@@ -1,0 +1,8 @@
+// Halo convolution kernels instantiated for __nv_bfloat16.
+#include "conv_launch_impl.cuh"
+
+namespace tsc {
+
+int launch_tch_bf16(const ConvArgs& a) { return detail::launch_tch<__nv_bfloat16>(a); }
+
+}  // namespace tsc

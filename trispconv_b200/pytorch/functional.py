@@ -12,7 +12,7 @@ from typing import Optional
 import torch
 
 from trispconv_b200 import _lib as L
-from trispconv_b200.pytorch.indices import IndiceData, KernelMap, build_row_order, kmap_from_pairs
+from trispconv_b200.pytorch.indices import IndiceData, KernelMap, build_row_order, build_tile_halo, kmap_from_pairs
 
 SUPPORTED_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 
@@ -33,6 +33,20 @@ if os.environ.get("TRISPCONV_B200_TC", "1") != "0":
 # itself cost 0.1-0.2 ms per map.
 ROW_ORDER_MIN_ROWS = 16384
 _ROW_ORDER = os.environ.get("TRISPCONV_B200_ROW_ORDER", "0") == "1"
+
+
+# TRISPCONV_B200_HALO=1 makes 64-channel 16-bit layers on the persistent
+# tcgen05 kernel stage each tile's distinct input rows once in shared memory
+# (tsc_tile_halo, built once per kernel map).  Off by default: on the
+# config-3 maps it moves 2.4x fewer bytes from L2 but runs slower than the
+# TMA-gather kernel (the halo load of a tile cannot overlap the previous
+# tile's MMAs within the shared memory left after two stages).
+_HALO = os.environ.get("TRISPCONV_B200_HALO", "0") == "1"
+
+
+def set_tile_halo(on: bool) -> None:
+    global _HALO
+    _HALO = bool(on)
 
 
 def set_row_order(on: bool) -> None:
@@ -116,12 +130,30 @@ def conv_launch(features: torch.Tensor, weight: torch.Tensor, weight_layout: int
     w = _as_dtype(weight, dtype)
     b = None if bias is None else _as_dtype(bias.reshape(-1), dtype)
     lib = L.load()
-    rc = lib.tsc_conv_forward(feats.data_ptr() if n_in else None, L.DTYPE_CODE[dtype], n_in, c_in,
-                              w.data_ptr(), weight_layout, L.ptr(b), L.ptr(gather), L.ptr(order), k_vol, n_out,
-                              c_out, L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(),
-                              (L.CONV_RELU if relu else 0) | _FORCE_FLAGS, L.status_word(dev).data_ptr(),
-                              L.tile_counter(dev).data_ptr(), L.stream_ptr(dev))
-    L.check(rc, "tsc_conv_forward")
+    flags = (L.CONV_RELU if relu else 0) | _FORCE_FLAGS
+    halo = None
+    if (_HALO and gather is not None and order is None and n_in > 0 and dtype != torch.float32
+            and weight_layout == L.W_KRSC and km.n_out == n_out):
+        hcap = lib.tsc_conv_halo_capacity(L.DTYPE_CODE[dtype], c_in, c_out, k_vol, flags)
+        if hcap > 0:
+            halo = km.halo
+            if halo is None or halo[0] != hcap:
+                halo = km.halo = build_tile_halo(km, hcap, n_in)
+    if halo is not None:
+        hcap, hrows, hcount, hmap = halo
+        rc = lib.tsc_conv_forward_halo(feats.data_ptr(), L.DTYPE_CODE[dtype], n_in, c_in, w.data_ptr(),
+                                       weight_layout, L.ptr(b), gather.data_ptr(), None, k_vol, n_out, c_out,
+                                       L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(), flags,
+                                       L.status_word(dev).data_ptr(), L.tile_counter(dev).data_ptr(),
+                                       hrows.data_ptr(), hcount.data_ptr(), hmap.data_ptr(), hcap,
+                                       L.stream_ptr(dev))
+        L.check(rc, "tsc_conv_forward_halo")
+    else:
+        rc = lib.tsc_conv_forward(feats.data_ptr() if n_in else None, L.DTYPE_CODE[dtype], n_in, c_in,
+                                  w.data_ptr(), weight_layout, L.ptr(b), L.ptr(gather), L.ptr(order), k_vol, n_out,
+                                  c_out, L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(), flags,
+                                  L.status_word(dev).data_ptr(), L.tile_counter(dev).data_ptr(), L.stream_ptr(dev))
+        L.check(rc, "tsc_conv_forward")
     if L.EAGER_CHECKS:
         L.check_device_status(dev)
     return out

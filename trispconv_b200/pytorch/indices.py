@@ -50,10 +50,12 @@ class KernelMap:
              reference-ordered pair lists.
     row_order int32 [n_out] or None: order in which the conv kernel groups
              output rows into tiles (does not change results).
+    halo     None or (capacity, rows, count, halo_map): per-tile input halos
+             (tsc_tile_halo) for the 64-channel tcgen05 conv kernel.
     """
 
     __slots__ = ("k_vol", "n_in", "n_out", "gather", "scatter", "overflow", "overflow_cap", "meta",
-                 "pair_map", "pair_mode", "pair_remap", "n_part", "device", "row_order")
+                 "pair_map", "pair_mode", "pair_remap", "n_part", "device", "row_order", "halo")
 
     def __init__(self, k_vol: int, n_in: int, n_out: int, gather: Optional[torch.Tensor],
                  meta: Optional[torch.Tensor], device: torch.device, *, scatter=None, overflow=None,
@@ -73,6 +75,25 @@ class KernelMap:
         self.n_part = n_part
         self.device = device
         self.row_order = row_order
+        self.halo = None
+
+
+def build_tile_halo(km: "KernelMap", capacity: int, n_in: int):
+    """Per-tile input halos of `km` (tsc_tile_halo) for a conv kernel holding
+    `capacity` rows per tile over `n_in` feature rows; cached on the map by
+    the caller."""
+    dev = km.device
+    n_out = km.n_out
+    tiles = (n_out + L.HALO_TILE_ROWS - 1) // L.HALO_TILE_ROWS
+    rows = torch.empty(tiles * capacity, dtype=torch.int32, device=dev)
+    count = torch.empty(tiles, dtype=torch.int32, device=dev)
+    hmap = torch.empty((km.k_vol, n_out), dtype=torch.int16, device=dev)
+    lib = L.load()
+    with L.on_device(dev):
+        L.check(lib.tsc_tile_halo(km.gather.data_ptr(), km.k_vol, n_in, n_out, capacity, rows.data_ptr(),
+                                  count.data_ptr(), hmap.data_ptr(), L.status_word(dev).data_ptr(),
+                                  L.stream_ptr(dev)), "tsc_tile_halo")
+    return (capacity, rows, count, hmap)
 
 
 def build_row_order(km: "KernelMap") -> torch.Tensor:
@@ -254,10 +275,22 @@ def _empty_strided(indices, K, shape, out_shape, ks, st, pd, dl) -> IndiceData:
                       kernel_size=ks, stride=st, padding=pd, dilation=dl, subm=False, kmap=km)
 
 
-def generate_strided_indice_pairs(indices: torch.Tensor, spatial_shape, batch_size: int, kernel_size,
-                                  stride=1, padding=0, dilation=1) -> IndiceData:
-    """Strided kernel map (indices.py:143-259): output coordinates sorted by
-    (b, z, y, x) key, pairs per offset in input-row order."""
+class PendingStrided:
+    """A strided kernel map whose first half is queued on the GPU: the count
+    kernels (tsc_strided_kmap_count) and a copy of the counts into pinned host
+    memory, with an event after the copy.  finish_strided_indice_pairs
+    completes it.  Splitting the build lets a caller queue other work (the
+    convolutions of earlier layers) between the halves, so the GPU keeps
+    working while the host waits for the output count."""
+
+    __slots__ = ("indices", "idx", "spatial_shape", "out_shape", "batch_size", "ks", "st", "pd", "dl", "K",
+                 "geo", "ws", "meta", "scatter", "host", "event", "stream")
+
+
+def start_strided_indice_pairs(indices: torch.Tensor, spatial_shape, batch_size: int, kernel_size,
+                               stride=1, padding=0, dilation=1):
+    """First half of generate_strided_indice_pairs: a PendingStrided, or the
+    finished (empty) IndiceData when there can be no output."""
     ks, st, pd, dl = _to3(kernel_size), _to3(stride), _to3(padding), _to3(dilation)
     shape = tuple(int(v) for v in spatial_shape)
     out_shape = _output_spatial_shape(shape, ks, st, pd, dl)
@@ -268,38 +301,69 @@ def generate_strided_indice_pairs(indices: torch.Tensor, spatial_shape, batch_si
     if n_in == 0 or min(out_shape) <= 0:
         return _empty_strided(indices, K, shape, out_shape, ks, st, pd, dl)
     lib = L.load()
-    geo = L.make_geometry(batch_size, shape, out_shape, ks, st, pd, dl)
-    ws = L.workspace(lib.tsc_strided_kmap_workspace(L.byref(geo)), dev)
-    meta = torch.empty(L.META_COUNTS + K, dtype=torch.int64, device=dev)
-    scatter = torch.empty((K, n_in), dtype=torch.int32, device=dev)  # size known before the count
-    status = L.status_word(dev)
-    stream = L.stream_ptr(dev)
+    p = PendingStrided()
+    p.indices, p.idx, p.spatial_shape, p.out_shape, p.batch_size = indices, idx, spatial_shape, out_shape, batch_size
+    p.ks, p.st, p.pd, p.dl, p.K = ks, st, pd, dl, K
+    p.geo = L.make_geometry(batch_size, shape, out_shape, ks, st, pd, dl)
+    p.ws = L.workspace(lib.tsc_strided_kmap_workspace(L.byref(p.geo)), dev)
+    p.meta = torch.empty(L.META_COUNTS + K, dtype=torch.int64, device=dev)
+    p.scatter = torch.empty((K, n_in), dtype=torch.int32, device=dev)  # size known before the count
+    p.stream = L.stream_ptr(dev)
     with L.on_device(dev):
-        L.check(lib.tsc_strided_kmap_count(idx.data_ptr(), n_in, L.byref(geo), ws.data_ptr(), ws.numel(),
-                                           meta.data_ptr(), status.data_ptr(), stream),
+        L.check(lib.tsc_strided_kmap_count(idx.data_ptr(), n_in, L.byref(p.geo), p.ws.data_ptr(), p.ws.numel(),
+                                           p.meta.data_ptr(), L.status_word(dev).data_ptr(), p.stream),
                 "tsc_strided_kmap_count")
-        host = meta.cpu().tolist()  # the one synchronisation: output count + status
-        L.raise_status(int(host[L.META_STATUS]), dev)
-        n_out = host[L.META_N_OUT]
-        n_part = host[L.META_N_PART]
-        counts = host[L.META_COUNTS:]
-        if n_out == 0:
-            return _empty_strided(indices, K, shape, out_shape, ks, st, pd, dl)
-        total_pairs = sum(counts)
-        out_indices = torch.empty((n_out, 4), dtype=torch.int32, device=dev)
-        gather = torch.empty((K, n_out), dtype=torch.int32, device=dev)
-        overflow = torch.empty((max(total_pairs, 1), 3), dtype=torch.int32, device=dev)
-        L.check(lib.tsc_strided_kmap_emit(idx.data_ptr(), n_in, L.byref(geo), ws.data_ptr(), ws.numel(),
+        p.host = torch.empty(p.meta.shape, dtype=torch.int64, pin_memory=True)
+        p.host.copy_(p.meta, non_blocking=True)
+        p.event = torch.cuda.Event()
+        p.event.record(torch.cuda.current_stream(dev))
+    return p
+
+
+def finish_strided_indice_pairs(p) -> IndiceData:
+    """Second half: waits for the output count (the one synchronisation of a
+    strided map), then emits coordinates, gather/scatter maps and overflow."""
+    if isinstance(p, IndiceData):
+        return p
+    p.event.synchronize()
+    host = p.host.tolist()
+    idx = p.idx
+    dev = idx.device
+    n_in = idx.shape[0]
+    K = p.K
+    L.raise_status(int(host[L.META_STATUS]), dev)
+    n_out = host[L.META_N_OUT]
+    n_part = host[L.META_N_PART]
+    counts = host[L.META_COUNTS:]
+    if n_out == 0:
+        return _empty_strided(p.indices, K, tuple(int(v) for v in p.spatial_shape), p.out_shape, p.ks, p.st, p.pd,
+                              p.dl)
+    total_pairs = sum(counts)
+    out_indices = torch.empty((n_out, 4), dtype=torch.int32, device=dev)
+    gather = torch.empty((K, n_out), dtype=torch.int32, device=dev)
+    overflow = torch.empty((max(total_pairs, 1), 3), dtype=torch.int32, device=dev)
+    lib = L.load()
+    with L.on_device(dev):
+        L.check(lib.tsc_strided_kmap_emit(idx.data_ptr(), n_in, L.byref(p.geo), p.ws.data_ptr(), p.ws.numel(),
                                           n_out, out_indices.data_ptr(), gather.data_ptr(),
-                                          scatter.data_ptr(), overflow.data_ptr(), overflow.shape[0],
-                                          meta.data_ptr(), status.data_ptr(), stream),
+                                          p.scatter.data_ptr(), overflow.data_ptr(), overflow.shape[0],
+                                          p.meta.data_ptr(), L.status_word(dev).data_ptr(), L.stream_ptr(dev)),
                 "tsc_strided_kmap_emit")
     _eager_check(dev)
-    km = KernelMap(K, n_in, n_out, gather, meta, dev, scatter=scatter, overflow=overflow,
-                   overflow_cap=overflow.shape[0], pair_map=scatter, pair_mode=1, n_part=n_part)
-    return IndiceData(out_indices=out_indices, pair_num=torch.tensor(counts, dtype=torch.long), input_indices=indices,
-                      input_spatial_shape=tuple(spatial_shape), output_spatial_shape=out_shape,
-                      kernel_size=ks, stride=st, padding=pd, dilation=dl, subm=False, kmap=km)
+    km = KernelMap(K, n_in, n_out, gather, p.meta, dev, scatter=p.scatter, overflow=overflow,
+                   overflow_cap=overflow.shape[0], pair_map=p.scatter, pair_mode=1, n_part=n_part)
+    return IndiceData(out_indices=out_indices, pair_num=torch.tensor(counts, dtype=torch.long),
+                      input_indices=p.indices, input_spatial_shape=tuple(p.spatial_shape),
+                      output_spatial_shape=p.out_shape, kernel_size=p.ks, stride=p.st, padding=p.pd,
+                      dilation=p.dl, subm=False, kmap=km)
+
+
+def generate_strided_indice_pairs(indices: torch.Tensor, spatial_shape, batch_size: int, kernel_size,
+                                  stride=1, padding=0, dilation=1) -> IndiceData:
+    """Strided kernel map (indices.py:143-259): output coordinates sorted by
+    (b, z, y, x) key, pairs per offset in input-row order."""
+    return finish_strided_indice_pairs(start_strided_indice_pairs(indices, spatial_shape, batch_size, kernel_size,
+                                                                  stride, padding, dilation))
 
 
 # --------------------------------------------------------------------------

@@ -18,16 +18,23 @@ from trispconv_b200 import _lib as L
 from trispconv_b200.pytorch.functional import check_features, conv_launch, kernel_map_for
 from trispconv_b200.pytorch.indices import (
     IndiceData,
+    PendingStrided,
     _to3,
+    finish_strided_indice_pairs,
     generate_strided_indice_pairs,
     generate_subm_indice_pairs,
     inverse_indice_data,
+    start_strided_indice_pairs,
 )
+from trispconv_b200.pytorch import kmap_stream
 from trispconv_b200.pytorch.kmap_stream import KmapScope, wait_ready
 from trispconv_b200.pytorch.tensor import SparseConvTensor
 from trispconv_b200.pytorch.weight import normalize_spconv_weight
 
 FUSE_RELU = os.environ.get("TRISPCONV_B200_FUSE", "1") != "0"
+# SparseSequential starts the count half of the next strided kernel map as
+# soon as its input coordinates exist (TRISPCONV_B200_LOOKAHEAD=0: off).
+LOOKAHEAD = os.environ.get("TRISPCONV_B200_LOOKAHEAD", "1") != "0"
 
 
 class SparseModule(nn.Module):
@@ -103,7 +110,7 @@ class SparseConvolution(SparseModule):
     def forward(self, x: SparseConvTensor) -> SparseConvTensor:
         return self._forward_impl(x, relu=False)
 
-    def _forward_impl(self, x: SparseConvTensor, relu: bool) -> SparseConvTensor:
+    def _forward_impl(self, x: SparseConvTensor, relu: bool, pending=None) -> SparseConvTensor:
         check_features(x.features)
         L.require_cuda(x.indices, "indices")
         with torch.no_grad():
@@ -111,7 +118,7 @@ class SparseConvolution(SparseModule):
                 return self._forward_inverse(x, relu)
             if self.subm:
                 return self._forward_subm(x, relu)
-            return self._forward_strided(x, relu)
+            return self._forward_strided(x, relu, pending)
 
     def _get_or_compute_subm_indice(self, x: SparseConvTensor) -> IndiceData:
         if self.indice_key is not None and self.indice_key in x.indice_dict:
@@ -124,13 +131,27 @@ class SparseConvolution(SparseModule):
             x.indice_dict[self.indice_key] = data
         return data
 
-    def _get_or_compute_strided_indice(self, x: SparseConvTensor) -> IndiceData:
+    def _start_strided_indice(self, x: SparseConvTensor):
+        """Count half of this layer's strided kernel map for input x (a
+        PendingStrided), or None when the map is cached or x has no device
+        coordinates."""
+        if self.subm or self.inverse or (self.indice_key is not None and self.indice_key in x.indice_dict):
+            return None
+        if not isinstance(x.indices, torch.Tensor) or not x.indices.is_cuda:
+            return None
+        return start_strided_indice_pairs(x.indices, tuple(x.spatial_shape), x.batch_size, self.kernel_size,
+                                          self.stride, self.padding, self.dilation)
+
+    def _get_or_compute_strided_indice(self, x: SparseConvTensor, pending=None) -> IndiceData:
         if self.indice_key is not None and self.indice_key in x.indice_dict:
             return x.indice_dict[self.indice_key]
-        with KmapScope(x.indices) as scope:
-            data = generate_strided_indice_pairs(x.indices, tuple(x.spatial_shape), x.batch_size,
-                                                 self.kernel_size, self.stride, self.padding, self.dilation)
-        scope.finish(data)
+        if pending is not None and pending.indices is x.indices:
+            data = finish_strided_indice_pairs(pending)
+        else:
+            with KmapScope(x.indices) as scope:
+                data = generate_strided_indice_pairs(x.indices, tuple(x.spatial_shape), x.batch_size,
+                                                     self.kernel_size, self.stride, self.padding, self.dilation)
+            scope.finish(data)
         if self.indice_key is not None:
             x.indice_dict[self.indice_key] = data
         return data
@@ -142,8 +163,8 @@ class SparseConvolution(SparseModule):
         return SparseConvTensor(out, data.out_indices, x.spatial_shape, x.batch_size,
                                 indice_dict=x.indice_dict)
 
-    def _forward_strided(self, x: SparseConvTensor, relu: bool = False) -> SparseConvTensor:
-        data = self._get_or_compute_strided_indice(x)
+    def _forward_strided(self, x: SparseConvTensor, relu: bool = False, pending=None) -> SparseConvTensor:
+        data = self._get_or_compute_strided_indice(x, pending)
         n_out = len(data.out_indices)
         out = self._conv(x.features, data, n_out, relu)
         return SparseConvTensor(out, data.out_indices, list(data.output_spatial_shape), x.batch_size,
@@ -201,6 +222,32 @@ class SparseInverseConv3d(SparseConvolution):
                          subm=False, inverse=True, indice_key=indice_key, algo=algo)
 
 
+def _plain_conv(m: nn.Module) -> bool:
+    """A SparseConvolution whose forward is the library's, without hooks."""
+    return (isinstance(m, SparseConvolution) and type(m).forward is SparseConvolution.forward
+            and not m._forward_hooks and not m._forward_pre_hooks)
+
+
+def _start_next_strided(mods, start: int, x: SparseConvTensor, pending: dict) -> None:
+    """Starts the count half of the first strided map at or after `start`
+    whose input will be x's coordinates: only submanifold convolutions and
+    dense (feature-only) modules may lie between."""
+    for j in range(start, len(mods)):
+        m = mods[j]
+        if isinstance(m, SparseConvolution):
+            if not _plain_conv(m) or m.inverse:
+                return
+            if m.subm:
+                continue
+            if id(m) not in pending:
+                p = m._start_strided_indice(x)
+                if isinstance(p, PendingStrided):
+                    pending[id(m)] = p
+            return
+        if isinstance(m, SparseModule):
+            return  # a sparse module of unknown effect on the coordinates
+
+
 def _fusable(conv: nn.Module, act: nn.Module) -> bool:
     """conv followed by a plain ReLU, no hooks, no forward override."""
     return (FUSE_RELU and isinstance(conv, SparseConvolution) and type(act) is nn.ReLU
@@ -233,15 +280,28 @@ class SparseSequential(SparseModule):
 
     def forward(self, x: Union[SparseConvTensor, torch.Tensor]) -> Union[SparseConvTensor, torch.Tensor]:
         mods = list(self.children())
+        # Strided kernel maps need their output count on the host.  Their
+        # count half is started as soon as the input coordinates exist, ahead
+        # of the convolutions of the layers before them, so that the host's
+        # wait for the count overlaps work already queued on the GPU.
+        lookahead = LOOKAHEAD and not kmap_stream.ENABLED
+        pending: dict = {}
+        scanned = None  # coordinates the look-ahead last started from
         i = 0
         while i < len(mods):
             module = mods[i]
             if isinstance(x, SparseConvTensor):
+                if lookahead and x.indices is not scanned:
+                    with torch.no_grad():
+                        _start_next_strided(mods, i, x, pending)
+                    scanned = x.indices
                 if i + 1 < len(mods) and _fusable(module, mods[i + 1]):
-                    x = module._forward_impl(x, relu=True)
+                    x = module._forward_impl(x, relu=True, pending=pending.pop(id(module), None))
                     i += 2
                     continue
-                if isinstance(module, SparseModule):
+                if id(module) in pending and _plain_conv(module):
+                    x = module._forward_impl(x, relu=False, pending=pending.pop(id(module)))
+                elif isinstance(module, SparseModule):
                     x = module(x)
                 else:
                     x = x.replace_feature(module(x.features))
