@@ -134,6 +134,15 @@ TSC_API size_t tsc_strided_kmap_workspace(const tsc_geometry* geo);
 TSC_API int tsc_strided_kmap_count(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
                            void* workspace, size_t workspace_bytes,
                            int64_t* meta, int64_t* status, void* stream);
+/* Step 1 with the counts also delivered to the host: the last count kernel
+ * copies meta[0 .. TSC_META_COUNTS + K) into host_meta, page-locked host
+ * memory the device can address (cudaHostAlloc / pinned tensors); other
+ * host memory gets an ordinary asynchronous copy on `stream`.  The caller
+ * waits on an event recorded after this call instead of copying meta back,
+ * which keeps the copy engine out of the stream. */
+TSC_API int tsc_strided_kmap_count_host(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
+                           void* workspace, size_t workspace_bytes,
+                           int64_t* meta, int64_t* host_meta, int64_t* status, void* stream);
 TSC_API int tsc_strided_kmap_emit(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
                           void* workspace, size_t workspace_bytes, int64_t n_out,
                           int32_t* out_indices, int32_t* gather_map, int32_t* scatter_map,

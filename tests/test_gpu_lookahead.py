@@ -121,3 +121,38 @@ def test_lookahead_stops_at_hooked_module_and_reuses_cached_maps(cuda):
     y2 = net(spconv.SparseConvTensor(f, idx, shape, 2, indice_dict=x.indice_dict))
     assert all(x.indice_dict[k] is maps[k] for k in maps)
     assert torch.equal(y1.features, y2.features)
+
+
+@pytest.mark.parametrize("pinned", [True, False], ids=["pinned", "pageable"])
+def test_count_host_delivers_meta(cuda, pinned):
+    """tsc_strided_kmap_count_host writes the same counts into host memory as
+    tsc_strided_kmap_count leaves in the device meta buffer (page-locked
+    memory through the kernel, other memory through a copy)."""
+    from trispconv_b200 import _lib as L
+
+    rng = np.random.default_rng(4)
+    shape = (16, 50, 50)
+    idx = torch.from_numpy(_cloud(rng, shape, 12_000)).to(cuda)
+    ks, st, pd, dl = (3, 3, 3), (2, 2, 2), (1, 1, 1), (1, 1, 1)
+    out_shape = tuple((s + 2 * p - d * (k - 1) - 1) // t + 1 for s, k, t, p, d in zip(shape, ks, st, pd, dl))
+    geo = L.make_geometry(2, shape, out_shape, ks, st, pd, dl)
+    lib = L.load()
+    n = L.META_COUNTS + 27
+    metas = []
+    host = (torch.zeros(n, dtype=torch.int64, pin_memory=True) if pinned else
+            torch.from_numpy(np.zeros(n, dtype=np.int64)))
+    for with_host in (False, True):
+        ws = L.workspace(lib.tsc_strided_kmap_workspace(L.byref(geo)), cuda)
+        meta = torch.empty(n, dtype=torch.int64, device=cuda)
+        args = (idx.data_ptr(), idx.shape[0], L.byref(geo), ws.data_ptr(), ws.numel(), meta.data_ptr())
+        if with_host:
+            rc = lib.tsc_strided_kmap_count_host(*args, host.data_ptr(), L.status_word(cuda).data_ptr(),
+                                                 L.stream_ptr(cuda))
+        else:
+            rc = lib.tsc_strided_kmap_count(*args, L.status_word(cuda).data_ptr(), L.stream_ptr(cuda))
+        L.check(rc, "count")
+        torch.cuda.synchronize()
+        metas.append(meta.cpu())
+    assert torch.equal(metas[0], metas[1])
+    assert torch.equal(host, metas[1])
+    assert int(host[L.META_N_OUT]) > 0

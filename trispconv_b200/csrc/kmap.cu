@@ -307,7 +307,8 @@ k_bitmap_tile_count(const uint4* __restrict__ bitmap, uint32_t* __restrict__ blo
 template <typename U>
 __global__ void __launch_bounds__(kScanBlockThreads)
 k_scan_tile_sums(U* __restrict__ sums, int64_t nblocks, unsigned long long* __restrict__ meta,
-                 int meta_slot, const int64_t* __restrict__ status) {
+                 int meta_slot, const int64_t* __restrict__ status,
+                 unsigned long long* __restrict__ host_meta = nullptr, int meta_len = 0) {
   __shared__ U ws[32];
   U carry = 0;
   for (int64_t base = 0; base < nblocks; base += blockDim.x) {
@@ -330,6 +331,13 @@ k_scan_tile_sums(U* __restrict__ sums, int64_t nblocks, unsigned long long* __re
       meta[meta_slot] = static_cast<unsigned long long>(carry);
       if (status != nullptr) meta[TSC_META_STATUS] = static_cast<unsigned long long>(*status);
     }
+  }
+  if (host_meta != nullptr && meta != nullptr) {
+    // the whole meta block (earlier kernels wrote the rest) into mapped host
+    // memory, visible to the host once this kernel has completed
+    __syncthreads();
+    for (int i = threadIdx.x; i < meta_len; i += blockDim.x) host_meta[i] = meta[i];
+    __threadfence_system();
   }
 }
 
@@ -770,9 +778,12 @@ size_t tsc_strided_kmap_workspace(const tsc_geometry* geo) {
   return strided_ws(*geo).bytes;
 }
 
-int tsc_strided_kmap_count(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
-                           void* workspace, size_t workspace_bytes, int64_t* meta, int64_t* status,
-                           void* stream_) {
+}  // extern "C"
+
+namespace {
+
+int strided_count(const int32_t* indices, int64_t n_in, const tsc_geometry* geo, void* workspace,
+                  size_t workspace_bytes, int64_t* meta, int64_t* host_meta, int64_t* status, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   int rc = check_geometry(geo, true);
   if (rc != TSC_OK) return rc;
@@ -806,10 +817,42 @@ int tsc_strided_kmap_count(const int32_t* indices, int64_t n_in, const tsc_geome
   k_bitmap_tile_count<<<static_cast<unsigned>(w.nblocks), kThreads, 0, stream>>>(
       reinterpret_cast<const uint4*>(bitmap), sums);
   TSC_LAUNCH_CHECK("k_bitmap_tile_count");
-  k_scan_tile_sums<uint32_t><<<1, kScanBlockThreads, 0, stream>>>(sums, w.nblocks, umeta,
-                                                                  TSC_META_N_OUT, status);
+  unsigned long long* dev_host_meta = nullptr;
+  if (host_meta != nullptr) {
+    // the device address of the caller's page-locked buffer (the same
+    // address under unified addressing); memory the device cannot address
+    // gets an ordinary copy instead
+    void* p = nullptr;
+    if (cudaHostGetDevicePointer(&p, host_meta, 0) == cudaSuccess && p != nullptr) {
+      dev_host_meta = static_cast<unsigned long long*>(p);
+    } else {
+      (void)cudaGetLastError();
+    }
+  }
+  k_scan_tile_sums<uint32_t><<<1, kScanBlockThreads, 0, stream>>>(sums, w.nblocks, umeta, TSC_META_N_OUT, status,
+                                                                  dev_host_meta, TSC_META_COUNTS + K);
   TSC_LAUNCH_CHECK("k_scan_tile_sums");
+  if (host_meta != nullptr && dev_host_meta == nullptr)
+    TSC_CUDA(cudaMemcpyAsync(host_meta, meta, sizeof(int64_t) * (TSC_META_COUNTS + K), cudaMemcpyDeviceToHost,
+                             stream));
   return TSC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tsc_strided_kmap_count(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
+                           void* workspace, size_t workspace_bytes, int64_t* meta, int64_t* status,
+                           void* stream) {
+  return strided_count(indices, n_in, geo, workspace, workspace_bytes, meta, nullptr, status, stream);
+}
+
+int tsc_strided_kmap_count_host(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
+                                void* workspace, size_t workspace_bytes, int64_t* meta, int64_t* host_meta,
+                                int64_t* status, void* stream) {
+  TSC_CHECK_ARG(host_meta != nullptr, "host_meta must not be NULL");
+  return strided_count(indices, n_in, geo, workspace, workspace_bytes, meta, host_meta, status, stream);
 }
 
 int tsc_strided_kmap_emit(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,

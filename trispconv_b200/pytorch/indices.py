@@ -14,6 +14,7 @@ synchronisation; a strided map synchronises once to learn its output count.
 """
 from __future__ import annotations
 
+import weakref
 from typing import List, Optional, Sequence, Tuple
 
 import torch
@@ -275,6 +276,30 @@ def _empty_strided(indices, K, shape, out_shape, ks, st, pd, dl) -> IndiceData:
                       kernel_size=ks, stride=st, padding=pd, dilation=dl, subm=False, kmap=km)
 
 
+class _HostMeta:
+    """Page-locked host buffers that the strided count kernel writes its
+    counts into, per device.  A buffer is handed out again only when the map
+    that used it has read it (or was dropped) and its event has completed, so
+    a kernel still writing one never meets a new reader."""
+
+    _pool: dict = {}
+
+    @classmethod
+    def take(cls, device: torch.device, n: int):
+        slots = cls._pool.setdefault(device.index, [])
+        for slot in slots:
+            if not slot["busy"] and slot["t"].numel() >= n and (slot["ev"] is None or slot["ev"].query()):
+                slot["busy"] = True
+                return slot
+        slot = {"t": torch.empty(max(n, 64), dtype=torch.int64, pin_memory=True), "ev": None, "busy": True}
+        slots.append(slot)
+        return slot
+
+    @staticmethod
+    def release(slot) -> None:
+        slot["busy"] = False
+
+
 class PendingStrided:
     """A strided kernel map whose first half is queued on the GPU: the count
     kernels (tsc_strided_kmap_count) and a copy of the counts into pinned host
@@ -284,7 +309,7 @@ class PendingStrided:
     working while the host waits for the output count."""
 
     __slots__ = ("indices", "idx", "spatial_shape", "out_shape", "batch_size", "ks", "st", "pd", "dl", "K",
-                 "geo", "ws", "meta", "scatter", "host", "event", "stream")
+                 "geo", "ws", "meta", "scatter", "slot", "event", "stream", "__weakref__")
 
 
 def start_strided_indice_pairs(indices: torch.Tensor, spatial_shape, batch_size: int, kernel_size,
@@ -309,14 +334,16 @@ def start_strided_indice_pairs(indices: torch.Tensor, spatial_shape, batch_size:
     p.meta = torch.empty(L.META_COUNTS + K, dtype=torch.int64, device=dev)
     p.scatter = torch.empty((K, n_in), dtype=torch.int32, device=dev)  # size known before the count
     p.stream = L.stream_ptr(dev)
+    p.slot = _HostMeta.take(dev, p.meta.numel())
+    weakref.finalize(p, _HostMeta.release, p.slot)
     with L.on_device(dev):
-        L.check(lib.tsc_strided_kmap_count(idx.data_ptr(), n_in, L.byref(p.geo), p.ws.data_ptr(), p.ws.numel(),
-                                           p.meta.data_ptr(), L.status_word(dev).data_ptr(), p.stream),
-                "tsc_strided_kmap_count")
-        p.host = torch.empty(p.meta.shape, dtype=torch.int64, pin_memory=True)
-        p.host.copy_(p.meta, non_blocking=True)
+        L.check(lib.tsc_strided_kmap_count_host(idx.data_ptr(), n_in, L.byref(p.geo), p.ws.data_ptr(),
+                                                p.ws.numel(), p.meta.data_ptr(), p.slot["t"].data_ptr(),
+                                                L.status_word(dev).data_ptr(), p.stream),
+                "tsc_strided_kmap_count_host")
         p.event = torch.cuda.Event()
         p.event.record(torch.cuda.current_stream(dev))
+    p.slot["ev"] = p.event
     return p
 
 
@@ -326,7 +353,8 @@ def finish_strided_indice_pairs(p) -> IndiceData:
     if isinstance(p, IndiceData):
         return p
     p.event.synchronize()
-    host = p.host.tolist()
+    host = p.slot["t"][:p.meta.numel()].tolist()
+    _HostMeta.release(p.slot)
     idx = p.idx
     dev = idx.device
     n_in = idx.shape[0]
