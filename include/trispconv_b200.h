@@ -115,6 +115,18 @@ TSC_API int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry*
                   void* workspace, size_t workspace_bytes,
                   int32_t* gather_map, int64_t* meta, int64_t* status, void* stream);
 
+/* Direct-address variant: the same map as tsc_subm_kmap from a caller-held
+ * int32 table of at least batch*D*H*W cells (table_cells) indexed by the
+ * packed key, which must hold -1 in every cell on entry and holds -1 again
+ * when the call's work has run (the call writes the cells of its voxels, reads
+ * the neighbours' cells and clears its cells).  The reference builds the same
+ * kind of table (int64, filled anew per call, indices.py:54-64); keeping it
+ * all -1 between calls makes a build cost O(n) instead of O(cells).  Calls
+ * sharing a table must be serialised on one stream. */
+TSC_API int tsc_subm_kmap_dense(const int32_t* indices, int64_t n, const tsc_geometry* geo,
+                  int32_t* table, int64_t table_cells,
+                  int32_t* gather_map, int64_t* meta, int64_t* status, void* stream);
+
 /* ---- strided kernel map --------------------------------------------------
  * Replaces generate_strided_indice_pairs (indices.py:143-259).  The output
  * set is found with an occupancy bitmap over the output grid (1 bit per

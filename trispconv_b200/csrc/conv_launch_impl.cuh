@@ -48,9 +48,8 @@ int launch_mmaw_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bia
   const int64_t row_tiles = ceil_div(n_out, mma::BM);
   const int64_t cap = static_cast<int64_t>(sm_count()) * occ;
   dim3 grid(static_cast<unsigned>(row_tiles < cap ? row_tiles : cap), static_cast<unsigned>(ceil_div(c_out, TN)));
-  kern<<<grid, mma::NT, smem, stream>>>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                        flags, status);
-  TSC_LAUNCH_CHECK("k_conv_mmaw");
+  TSC_LAUNCH_PDL("k_conv_mmaw", kern, grid, dim3(mma::NT), smem, stream, f, n_in, c_in, w, bias, gmap, perm, K,
+                 n_out, c_out, ovf, ovf_cap, meta, out, flags, status);
   return TSC_OK;
 }
 
@@ -72,9 +71,8 @@ int launch_mma_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias
     configured |= 1ull << (dev & 63);
   }
   dim3 grid(static_cast<unsigned>(ceil_div(n_out, mma::BM)), static_cast<unsigned>(ceil_div(c_out, TN)));
-  kern<<<grid, mma::NT, C::bytes(K), stream>>>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap,
-                                               meta, out, flags, status);
-  TSC_LAUNCH_CHECK("k_conv_mma");
+  TSC_LAUNCH_PDL("k_conv_mma", kern, grid, dim3(mma::NT), C::bytes(K), stream, f, n_in, c_in, w, bias, gmap, perm,
+                 K, n_out, c_out, ovf, ovf_cap, meta, out, flags, status);
   return TSC_OK;
 }
 
@@ -206,11 +204,13 @@ int launch_tcp_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias
   }
   const int64_t tiles = ceil_div(n_out, tcp::BMT) * ceil_div(c_out, TN);
   const int64_t grid = tiles < sm_count() ? tiles : sm_count();
-  if (tile_counter != nullptr) TSC_CUDA(cudaMemsetAsync(tile_counter, 0, sizeof(uint32_t), stream));
-  kern<<<static_cast<unsigned>(grid), tcp::NT, C::TOTAL, stream>>>(mf, mw, f, n_in, c_in, w, bias, gmap, perm, K,
-                                                                  n_out, c_out, ovf, ovf_cap, meta, out, flags,
-                                                                  status, tile_counter);
-  TSC_LAUNCH_CHECK("k_conv_tcp");
+  if (tile_counter != nullptr) {
+    rc = fill_words(tile_counter, 0u, 1, nullptr, 0u, 0, stream);
+    if (rc != TSC_OK) return rc;
+  }
+  TSC_LAUNCH_PDL("k_conv_tcp", kern, dim3(static_cast<unsigned>(grid)), dim3(tcp::NT), C::TOTAL, stream, mf, mw, f,
+                 n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out, flags, status,
+                 tile_counter);
   return TSC_OK;
 }
 
@@ -268,12 +268,14 @@ int launch_tch_tn(const ConvArgs& a) {
   }
   const int64_t tiles = ceil_div(a.n_out, tch::BMT) * ceil_div(a.c_out, TN);
   const int64_t grid = tiles < sm_count() ? tiles : sm_count();
-  if (a.tile_counter != nullptr) TSC_CUDA(cudaMemsetAsync(a.tile_counter, 0, sizeof(uint32_t), a.stream));
-  kern<<<static_cast<unsigned>(grid), tch::NT, C::TOTAL, a.stream>>>(
-      mf, mw, f, a.n_in, w, static_cast<const T*>(a.bias), a.gather_map, a.k_vol, a.n_out, a.c_out, a.overflow,
-      a.overflow_cap, a.meta, static_cast<T*>(a.out), a.flags, a.status, a.tile_counter, a.halo_rows, a.halo_count,
-      a.halo_map);
-  TSC_LAUNCH_CHECK("k_conv_tch");
+  if (a.tile_counter != nullptr) {
+    rc = fill_words(a.tile_counter, 0u, 1, nullptr, 0u, 0, a.stream);
+    if (rc != TSC_OK) return rc;
+  }
+  TSC_LAUNCH_PDL("k_conv_tch", kern, dim3(static_cast<unsigned>(grid)), dim3(tch::NT), C::TOTAL, a.stream, mf, mw, f,
+                 a.n_in, w, static_cast<const T*>(a.bias), a.gather_map, a.k_vol, a.n_out, a.c_out, a.overflow,
+                 a.overflow_cap, a.meta, static_cast<T*>(a.out), a.flags, a.status, a.tile_counter, a.halo_rows,
+                 a.halo_count, a.halo_map);
   return TSC_OK;
 }
 

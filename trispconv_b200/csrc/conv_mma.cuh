@@ -103,6 +103,8 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
            const T* __restrict__ bias, const int32_t* __restrict__ gmap, const int32_t* __restrict__ perm,
            int K, int64_t n_out, int c_out, const int32_t* __restrict__ ovf, int64_t ovf_cap,
            const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   using C = Cfg<TN, KC>;
   constexpr int WN = (TN == 128) ? 2 : 1;
   constexpr int WM = 8 / WN;
@@ -334,6 +336,8 @@ k_conv_mmaw(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict
             const T* __restrict__ bias, const int32_t* __restrict__ gmap, const int32_t* __restrict__ perm,
             int K, int64_t n_out, int c_out, const int32_t* __restrict__ ovf, int64_t ovf_cap,
             const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   using C = CfgW<TN, KC>;
   constexpr int WN = (TN == 128) ? 2 : 1;
   constexpr int WM = 8 / WN;

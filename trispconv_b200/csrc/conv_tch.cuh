@@ -133,6 +133,8 @@ k_conv_tch(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
            int64_t* __restrict__ status, unsigned* __restrict__ tile_counter,
            const int32_t* __restrict__ halo_rows, const int32_t* __restrict__ halo_count,
            const int16_t* __restrict__ hmap) {
+  pdl_wait();
+  pdl_trigger();
   using C = Cfg<TN>;
   constexpr int NACC = C::NACC;
   constexpr int HALO = C::HALO;

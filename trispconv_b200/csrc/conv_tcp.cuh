@@ -131,6 +131,8 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
            int64_t n_out, int c_out, const int32_t* __restrict__ ovf, int64_t ovf_cap,
            const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status,
            unsigned* __restrict__ tile_counter) {
+  pdl_wait();
+  pdl_trigger();
   using C = Cfg<TN, KC>;
   constexpr int NS = C::NS;
   constexpr int NACC = C::NACC;

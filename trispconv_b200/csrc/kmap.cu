@@ -79,6 +79,8 @@ __device__ __forceinline__ uint32_t cell_key(unsigned b, unsigned z, unsigned y,
 __global__ void __launch_bounds__(kThreads)
 k_hash_build(const int4* __restrict__ idx, int64_t n, int B, int D, int H, int W,
              unsigned long long* __restrict__ table, int log2cap, int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int4 c = idx[i];
@@ -121,13 +123,28 @@ __device__ __forceinline__ int hash_lookup(const unsigned long long* __restrict_
   return -1;
 }
 
+// Lookups of a packed cell key: in the open-addressing hash, or in a
+// direct-address table (one int32 row per cell, -1 = empty).
+struct HashLookup {
+  const unsigned long long* table;
+  int log2cap;
+  __device__ __forceinline__ int operator()(uint32_t key) const { return hash_lookup(table, log2cap, key); }
+};
+
+struct DenseLookup {
+  const int32_t* table;
+  __device__ __forceinline__ int operator()(uint32_t key) const { return __ldg(&table[key]); }
+};
+
 // One thread per (offset k = blockIdx.y, row i).  Writes gather_map[k][i] and
 // accumulates pair_num[k].  Offsets follow indices.py:96-98:
 // (k_dim - K_dim//2) * dilation.
+template <class Lookup>
 __global__ void __launch_bounds__(kThreads)
-k_subm_query(const int4* __restrict__ idx, int64_t n, GeoDev g,
-             const unsigned long long* __restrict__ table, int log2cap,
+k_subm_query(const int4* __restrict__ idx, int64_t n, GeoDev g, Lookup look,
              int32_t* __restrict__ gmap, unsigned long long* __restrict__ meta) {
+  pdl_wait();
+  pdl_trigger();
   const int k = blockIdx.y;
   const KOffset ko = split_k(k, g.kH, g.kW);
   const int offz = (ko.kz - g.kD / 2) * g.dz;
@@ -142,7 +159,7 @@ k_subm_query(const int4* __restrict__ idx, int64_t n, GeoDev g,
         static_cast<unsigned>(nz) < static_cast<unsigned>(g.D) &&
         static_cast<unsigned>(ny) < static_cast<unsigned>(g.H) &&
         static_cast<unsigned>(nx) < static_cast<unsigned>(g.W)) {
-      found = hash_lookup(table, log2cap, cell_key(c.x, nz, ny, nx, g.D, g.H, g.W));
+      found = look(cell_key(c.x, nz, ny, nx, g.D, g.H, g.W));
     }
     gmap[static_cast<int64_t>(k) * n + i] = found;
   }
@@ -158,10 +175,12 @@ k_subm_query(const int4* __restrict__ idx, int64_t n, GeoDev g,
 // offset and block.
 constexpr int kRowQueryKMax = 128;
 
+template <class Lookup>
 __global__ void __launch_bounds__(kThreads)
-k_subm_query_rows(const int4* __restrict__ idx, int64_t n, GeoDev g,
-                  const unsigned long long* __restrict__ table, int log2cap,
+k_subm_query_rows(const int4* __restrict__ idx, int64_t n, GeoDev g, Lookup look,
                   int32_t* __restrict__ gmap, unsigned long long* __restrict__ meta) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ unsigned s_cnt[kRowQueryKMax];
   const int K = g.kD * g.kH * g.kW;
   for (int t = threadIdx.x; t < K; t += blockDim.x) s_cnt[t] = 0u;
@@ -183,7 +202,7 @@ k_subm_query_rows(const int4* __restrict__ idx, int64_t n, GeoDev g,
         const int nx = c.w + (kx - g.kW / 2) * g.dx;
         int found = -1;
         if (zy_ok && static_cast<unsigned>(nx) < static_cast<unsigned>(g.W))
-          found = hash_lookup(table, log2cap, cell_key(c.x, nz, ny, nx, g.D, g.H, g.W));
+          found = look(cell_key(c.x, nz, ny, nx, g.D, g.H, g.W));
         if (row) gmap[static_cast<int64_t>(k) * n + i] = found;
         const unsigned hits = __ballot_sync(kFullMask, found >= 0);
         if (lane == 0 && hits) atomicAdd(&s_cnt[k], static_cast<unsigned>(__popc(hits)));
@@ -195,22 +214,54 @@ k_subm_query_rows(const int4* __restrict__ idx, int64_t n, GeoDev g,
     if (s_cnt[t]) atomicAdd(&meta[TSC_META_COUNTS + t], static_cast<unsigned long long>(s_cnt[t]));
 }
 
-// Builds gather_map and pair_num from a filled hash table (both the
-// workspace and the allocation-free entry points).
-int launch_subm_query(const int4* idx, int64_t n, const GeoDev& g, const unsigned long long* table, int log2cap,
-                      int32_t* gmap, int64_t* meta, cudaStream_t stream) {
+// Builds gather_map and pair_num from a filled hash or direct-address table
+// (the workspace, allocation-free and dense entry points).
+template <class Lookup>
+int launch_subm_query(const int4* idx, int64_t n, const GeoDev& g, Lookup look, int32_t* gmap, int64_t* meta,
+                      cudaStream_t stream) {
   const int K = g.kD * g.kH * g.kW;
   const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
   if (K <= kRowQueryKMax) {
-    k_subm_query_rows<<<grid, kThreads, 0, stream>>>(idx, n, g, table, log2cap, gmap,
-                                                     reinterpret_cast<unsigned long long*>(meta));
-    TSC_LAUNCH_CHECK("k_subm_query_rows");
+    TSC_LAUNCH_PDL("k_subm_query_rows", k_subm_query_rows<Lookup>, dim3(grid), dim3(kThreads), 0, stream, idx, n, g,
+                   look, gmap, reinterpret_cast<unsigned long long*>(meta));
   } else {
-    k_subm_query<<<dim3(grid, K), kThreads, 0, stream>>>(idx, n, g, table, log2cap, gmap,
-                                                         reinterpret_cast<unsigned long long*>(meta));
-    TSC_LAUNCH_CHECK("k_subm_query");
+    TSC_LAUNCH_PDL("k_subm_query", k_subm_query<Lookup>, dim3(grid, K), dim3(kThreads), 0, stream, idx, n, g, look,
+                   gmap, reinterpret_cast<unsigned long long*>(meta));
   }
   return TSC_OK;
+}
+
+int launch_subm_query(const int4* idx, int64_t n, const GeoDev& g, const unsigned long long* table, int log2cap,
+                      int32_t* gmap, int64_t* meta, cudaStream_t stream) {
+  return launch_subm_query(idx, n, g, HashLookup{table, log2cap}, gmap, meta, stream);
+}
+
+// Direct-address table: the largest row of each cell (the reference's
+// last-write-wins `table[key] = arange(N)`, indices.py:63) over cells that
+// hold -1; k_dense_clear puts -1 back into the same cells afterwards.
+__global__ void __launch_bounds__(kThreads)
+k_dense_build(const int4* __restrict__ idx, int64_t n, int B, int D, int H, int W, int32_t* __restrict__ table,
+              int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int4 c = idx[i];
+  if (!in_grid(c, B, D, H, W)) {
+    raise_status(status, TSC_STATUS_KEY_RANGE);
+    return;
+  }
+  atomicMax(&table[cell_key(c.x, c.y, c.z, c.w, D, H, W)], static_cast<int32_t>(i));
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_dense_clear(const int4* __restrict__ idx, int64_t n, int B, int D, int H, int W, int32_t* __restrict__ table) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int4 c = idx[i];
+  if (in_grid(c, B, D, H, W)) table[cell_key(c.x, c.y, c.z, c.w, D, H, W)] = -1;
 }
 
 // ---------------------------------------------------------------------------
@@ -239,6 +290,8 @@ __device__ __forceinline__ bool exact_div(int c, int s, int lim, int& o) {
 __global__ void __launch_bounds__(kThreads)
 k_strided_mark(const int4* __restrict__ idx, int64_t n, GeoDev g, uint32_t* __restrict__ bitmap,
                unsigned long long* __restrict__ meta, int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ unsigned int s_cnt[];  // K pair counters + 1 participation counter
   const int K = g.kD * g.kH * g.kW;
   for (int t = threadIdx.x; t <= K; t += blockDim.x) s_cnt[t] = 0u;
@@ -292,6 +345,8 @@ k_strided_mark(const int4* __restrict__ idx, int64_t n, GeoDev g, uint32_t* __re
 // Popcount of each 2048-word tile of the (zero-padded) bitmap.
 __global__ void __launch_bounds__(kThreads)
 k_bitmap_tile_count(const uint4* __restrict__ bitmap, uint32_t* __restrict__ block_sums) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ uint32_t ws[32];
   const size_t q = (static_cast<size_t>(blockIdx.x) * kTile + threadIdx.x * kItems) / 4;
   const uint4 a = bitmap[q], b = bitmap[q + 1];
@@ -309,6 +364,8 @@ __global__ void __launch_bounds__(kScanBlockThreads)
 k_scan_tile_sums(U* __restrict__ sums, int64_t nblocks, unsigned long long* __restrict__ meta,
                  int meta_slot, const int64_t* __restrict__ status,
                  unsigned long long* __restrict__ host_meta = nullptr, int meta_len = 0) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ U ws[32];
   U carry = 0;
   for (int64_t base = 0; base < nblocks; base += blockDim.x) {
@@ -348,6 +405,8 @@ k_scan_tile_sums(U* __restrict__ sums, int64_t nblocks, unsigned long long* __re
 __global__ void __launch_bounds__(kThreads)
 k_bitmap_prefix(const uint4* __restrict__ bitmap, const uint32_t* __restrict__ tile_off,
                 uint32_t* __restrict__ word_prefix) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ uint32_t ws[32];
   const size_t w0 = static_cast<size_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
   const uint4 a = bitmap[w0 / 4], b = bitmap[w0 / 4 + 1];
@@ -374,6 +433,8 @@ k_bitmap_prefix(const uint4* __restrict__ bitmap, const uint32_t* __restrict__ t
 __global__ void __launch_bounds__(kThreads)
 k_bitmap_coords(const uint32_t* __restrict__ bitmap, const uint32_t* __restrict__ word_prefix,
                 int64_t nwords, GeoDev g, int4* __restrict__ out_idx, int64_t n_out) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (w >= nwords) return;
   uint32_t wv = __ldg(&bitmap[w]);
@@ -422,6 +483,8 @@ k_strided_pairs(const int4* __restrict__ idx, int64_t n, GeoDev g,
                 int64_t n_out, int32_t* __restrict__ gmap, int32_t* __restrict__ smap,
                 int32_t* __restrict__ overflow, int64_t ovf_cap,
                 unsigned long long* __restrict__ meta, int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int4 c = __ldg(&idx[i]);
@@ -471,6 +534,8 @@ __device__ __forceinline__ bool row_participates(const int32_t* __restrict__ map
 
 __global__ void __launch_bounds__(kThreads)
 k_part_tile_count(const int32_t* __restrict__ map, int K, int64_t n, uint32_t* __restrict__ block_sums) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ uint32_t ws[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
   uint32_t s = 0;
@@ -491,6 +556,8 @@ k_inverse_strided_emit(const int4* __restrict__ in_idx, const int32_t* __restric
                        int64_t n, const uint32_t* __restrict__ tile_off, int64_t n_part,
                        int4* __restrict__ out_idx, int32_t* __restrict__ inv_gather,
                        int32_t* __restrict__ compact) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ uint32_t ws[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
   bool flag[kItems];
@@ -519,6 +586,8 @@ k_inverse_strided_emit(const int4* __restrict__ in_idx, const int32_t* __restric
 
 __global__ void __launch_bounds__(kThreads)
 k_iota(int32_t* __restrict__ out, int64_t n) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n) out[i] = static_cast<int32_t>(i);
 }
@@ -526,6 +595,8 @@ k_iota(int32_t* __restrict__ out, int64_t n) {
 // Inverse of a submanifold map: flag every row j read by some pair.
 __global__ void __launch_bounds__(kThreads)
 k_flag_targets(const int32_t* __restrict__ gmap, int64_t total, int64_t n, int32_t* __restrict__ flags) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (e >= total) return;
   const int j = gmap[e];
@@ -534,6 +605,8 @@ k_flag_targets(const int32_t* __restrict__ gmap, int64_t total, int64_t n, int32
 
 __global__ void __launch_bounds__(kThreads)
 k_flag_tile_count(const int32_t* __restrict__ flags, int64_t n, uint32_t* __restrict__ block_sums) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ uint32_t ws[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
   uint32_t s = 0;
@@ -550,6 +623,8 @@ k_flag_tile_count(const int32_t* __restrict__ flags, int64_t n, uint32_t* __rest
 // flags (0/1) -> compact ids (r or -1), in place.
 __global__ void __launch_bounds__(kThreads)
 k_flag_compact(int32_t* __restrict__ flags, int64_t n, const uint32_t* __restrict__ tile_off) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ uint32_t ws[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
   int32_t f[kItems];
@@ -575,6 +650,8 @@ k_flag_compact(int32_t* __restrict__ flags, int64_t n, const uint32_t* __restric
 __global__ void __launch_bounds__(kThreads)
 k_gather_rows(const int4* __restrict__ in_idx, const int32_t* __restrict__ compact, int64_t n,
               int64_t n_part, int4* __restrict__ out_idx) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int r = compact[i];
@@ -586,6 +663,8 @@ __global__ void __launch_bounds__(kThreads)
 k_transpose_map(const int32_t* __restrict__ gmap, int K, int64_t n, const int32_t* __restrict__ compact,
                 int64_t n_part, int32_t* __restrict__ inv_gather, int32_t* __restrict__ overflow,
                 int64_t ovf_cap, unsigned long long* __restrict__ meta, int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (e >= static_cast<int64_t>(K) * n) return;
   const int j = gmap[e];
@@ -604,6 +683,8 @@ k_transpose_map(const int32_t* __restrict__ gmap, int K, int64_t n, const int32_
 
 __global__ void __launch_bounds__(kThreads)
 k_map_tile_count(const int32_t* __restrict__ map, int64_t total, unsigned long long* __restrict__ block_sums) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ uint32_t ws[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
   uint32_t s = 0;
@@ -621,6 +702,8 @@ __global__ void __launch_bounds__(kThreads)
 k_map_emit_pairs(const int32_t* __restrict__ map, int64_t total, int64_t n, int mode,
                  const int32_t* __restrict__ remap, const unsigned long long* __restrict__ tile_off,
                  int64_t* __restrict__ pairs_in, int64_t* __restrict__ pairs_out, int64_t capacity) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ uint32_t ws[32];
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
   int32_t v[kItems];
@@ -655,6 +738,8 @@ __global__ void __launch_bounds__(kThreads)
 k_pairs_to_gather(const int64_t* __restrict__ pin, const int64_t* __restrict__ pout, int64_t count,
                   int k, int64_t n_out, int32_t* __restrict__ gmap, int32_t* __restrict__ overflow,
                   int64_t ovf_cap, unsigned long long* __restrict__ meta, int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (p >= count) return;
   const int64_t o = pout[p];
@@ -753,8 +838,8 @@ int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo, vo
     return TSC_ERR_GRID_TOO_LARGE;
   }
   const int K = geo->ksize[0] * geo->ksize[1] * geo->ksize[2];
-  TSC_CUDA(cudaMemsetAsync(meta, 0, sizeof(int64_t) * (TSC_META_COUNTS + K), stream));
-  if (n == 0) return TSC_OK;
+  const int64_t meta_words = 2 * static_cast<int64_t>(TSC_META_COUNTS + K);
+  if (n == 0) return fill_words(meta, 0u, meta_words, nullptr, 0u, 0, stream);
   TSC_CHECK_ARG(indices != nullptr && aligned(indices, 16), "indices must be 16-byte aligned");
   TSC_CHECK_ARG(gather_map != nullptr && aligned(gather_map, 4), "gather_map must not be NULL");
   const int log2cap = subm_log2cap(n);
@@ -764,13 +849,47 @@ int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo, vo
     return TSC_ERR_WORKSPACE;
   }
   auto* table = static_cast<unsigned long long*>(workspace);
-  TSC_CUDA(cudaMemsetAsync(table, 0xFF, need, stream));
+  // meta = 0 and every table slot empty (all ones), one launch
+  rc = fill_words(meta, 0u, meta_words, table, 0xFFFFFFFFu, static_cast<int64_t>(need / 4), stream);
+  if (rc != TSC_OK) return rc;
   const GeoDev g = to_dev(*geo);
   const int4* idx = reinterpret_cast<const int4*>(indices);
   const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
-  k_hash_build<<<grid, kThreads, 0, stream>>>(idx, n, g.B, g.D, g.H, g.W, table, log2cap, status);
-  TSC_LAUNCH_CHECK("k_hash_build");
+  TSC_LAUNCH_PDL("k_hash_build", k_hash_build, dim3(grid), dim3(kThreads), 0, stream, idx, n, g.B, g.D, g.H, g.W,
+                 table, log2cap, status);
   return launch_subm_query(idx, n, g, table, log2cap, gather_map, meta, stream);
+}
+
+int tsc_subm_kmap_dense(const int32_t* indices, int64_t n, const tsc_geometry* geo, int32_t* table,
+                        int64_t table_cells, int32_t* gather_map, int64_t* meta, int64_t* status, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int rc = check_geometry(geo, false);
+  if (rc != TSC_OK) return rc;
+  TSC_CHECK_ARG(n >= 0 && n <= 0x7fffffffLL, "number of voxels %lld out of range", (long long)n);
+  TSC_CHECK_ARG(meta != nullptr && status != nullptr, "meta/status must not be NULL");
+  const uint64_t cells = cells_of(geo->batch, geo->in_shape);
+  if (cells > kMaxCells) {
+    set_error("grid batch*D*H*W = %llu exceeds the packed-key limit 2^32-2", (unsigned long long)cells);
+    return TSC_ERR_GRID_TOO_LARGE;
+  }
+  TSC_CHECK_ARG(table != nullptr && table_cells >= 0 && static_cast<uint64_t>(table_cells) >= cells,
+                "dense table holds %lld cells, the grid has %llu", (long long)table_cells,
+                (unsigned long long)cells);
+  const int K = geo->ksize[0] * geo->ksize[1] * geo->ksize[2];
+  rc = fill_words(meta, 0u, 2 * static_cast<int64_t>(TSC_META_COUNTS + K), nullptr, 0u, 0, stream);
+  if (rc != TSC_OK || n == 0) return rc;
+  TSC_CHECK_ARG(indices != nullptr && aligned(indices, 16), "indices must be 16-byte aligned");
+  TSC_CHECK_ARG(gather_map != nullptr && aligned(gather_map, 4), "gather_map must not be NULL");
+  const GeoDev g = to_dev(*geo);
+  const int4* idx = reinterpret_cast<const int4*>(indices);
+  const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
+  TSC_LAUNCH_PDL("k_dense_build", k_dense_build, dim3(grid), dim3(kThreads), 0, stream, idx, n, g.B, g.D, g.H, g.W,
+                 table, status);
+  rc = launch_subm_query(idx, n, g, DenseLookup{table}, gather_map, meta, stream);
+  if (rc != TSC_OK) return rc;
+  TSC_LAUNCH_PDL("k_dense_clear", k_dense_clear, dim3(grid), dim3(kThreads), 0, stream, idx, n, g.B, g.D, g.H, g.W,
+                 table);
+  return TSC_OK;
 }
 
 size_t tsc_strided_kmap_workspace(const tsc_geometry* geo) {
@@ -805,18 +924,18 @@ int strided_count(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
   auto* bitmap = reinterpret_cast<uint32_t*>(ws);
   auto* sums = reinterpret_cast<uint32_t*>(ws + w.off_sums);
   auto* umeta = reinterpret_cast<unsigned long long*>(meta);
-  TSC_CUDA(cudaMemsetAsync(meta, 0, sizeof(int64_t) * (TSC_META_COUNTS + K), stream));
-  TSC_CUDA(cudaMemsetAsync(bitmap, 0, static_cast<size_t>(w.nwords_pad) * 4, stream));
+  // meta = 0 and an empty occupancy bitmap, one launch
+  int rc2 = fill_words(meta, 0u, 2 * static_cast<int64_t>(TSC_META_COUNTS + K), bitmap, 0u,
+                       static_cast<int64_t>(w.nwords_pad), stream);
+  if (rc2 != TSC_OK) return rc2;
   const GeoDev g = to_dev(*geo);
   if (n_in > 0) {
     const unsigned grid = static_cast<unsigned>(ceil_div(n_in, kThreads));
-    k_strided_mark<<<grid, kThreads, sizeof(unsigned) * (K + 1), stream>>>(
-        reinterpret_cast<const int4*>(indices), n_in, g, bitmap, umeta, status);
-    TSC_LAUNCH_CHECK("k_strided_mark");
+    TSC_LAUNCH_PDL("k_strided_mark", k_strided_mark, dim3(grid), dim3(kThreads), sizeof(unsigned) * (K + 1), stream,
+                   reinterpret_cast<const int4*>(indices), n_in, g, bitmap, umeta, status);
   }
-  k_bitmap_tile_count<<<static_cast<unsigned>(w.nblocks), kThreads, 0, stream>>>(
-      reinterpret_cast<const uint4*>(bitmap), sums);
-  TSC_LAUNCH_CHECK("k_bitmap_tile_count");
+  TSC_LAUNCH_PDL("k_bitmap_tile_count", k_bitmap_tile_count, dim3(static_cast<unsigned>(w.nblocks)), dim3(kThreads), 0,
+                 stream, reinterpret_cast<const uint4*>(bitmap), sums);
   unsigned long long* dev_host_meta = nullptr;
   if (host_meta != nullptr) {
     // the device address of the caller's page-locked buffer (the same
@@ -829,9 +948,9 @@ int strided_count(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
       (void)cudaGetLastError();
     }
   }
-  k_scan_tile_sums<uint32_t><<<1, kScanBlockThreads, 0, stream>>>(sums, w.nblocks, umeta, TSC_META_N_OUT, status,
-                                                                  dev_host_meta, TSC_META_COUNTS + K);
-  TSC_LAUNCH_CHECK("k_scan_tile_sums");
+  TSC_LAUNCH_PDL("k_scan_tile_sums", k_scan_tile_sums<uint32_t>, dim3(1), dim3(kScanBlockThreads), 0, stream, sums,
+                 w.nblocks, umeta, TSC_META_N_OUT, static_cast<const int64_t*>(status), dev_host_meta,
+                 TSC_META_COUNTS + K);
   if (host_meta != nullptr && dev_host_meta == nullptr)
     TSC_CUDA(cudaMemcpyAsync(host_meta, meta, sizeof(int64_t) * (TSC_META_COUNTS + K), cudaMemcpyDeviceToHost,
                              stream));
@@ -881,20 +1000,21 @@ int tsc_strided_kmap_emit(const int32_t* indices, int64_t n_in, const tsc_geomet
   auto* prefix = reinterpret_cast<uint32_t*>(ws + w.off_prefix);
   auto* sums = reinterpret_cast<uint32_t*>(ws + w.off_sums);
   const GeoDev g = to_dev(*geo);
-  k_bitmap_prefix<<<static_cast<unsigned>(w.nblocks), kThreads, 0, stream>>>(
-      reinterpret_cast<const uint4*>(bitmap), sums, prefix);
-  TSC_LAUNCH_CHECK("k_bitmap_prefix");
+  // gather map = -1 and the overflow count = 0, one launch
+  rc = fill_words(gather_map, 0xFFFFFFFFu, static_cast<int64_t>(K) * n_out, meta + TSC_META_N_OVERFLOW, 0u, 2,
+                  stream);
+  if (rc != TSC_OK) return rc;
+  TSC_LAUNCH_PDL("k_bitmap_prefix", k_bitmap_prefix, dim3(static_cast<unsigned>(w.nblocks)), dim3(kThreads), 0,
+                 stream, reinterpret_cast<const uint4*>(bitmap), static_cast<const uint32_t*>(sums), prefix);
   const int64_t nwords = static_cast<int64_t>((w.nbits + 31) / 32);
-  k_bitmap_coords<<<static_cast<unsigned>(ceil_div(nwords, kThreads)), kThreads, 0, stream>>>(
-      bitmap, prefix, nwords, g, reinterpret_cast<int4*>(out_indices), n_out);
-  TSC_LAUNCH_CHECK("k_bitmap_coords");
-  TSC_CUDA(cudaMemsetAsync(gather_map, 0xFF, sizeof(int32_t) * static_cast<size_t>(K) * n_out, stream));
-  TSC_CUDA(cudaMemsetAsync(meta + TSC_META_N_OVERFLOW, 0, sizeof(int64_t), stream));
+  TSC_LAUNCH_PDL("k_bitmap_coords", k_bitmap_coords, dim3(static_cast<unsigned>(ceil_div(nwords, kThreads))),
+                 dim3(kThreads), 0, stream, static_cast<const uint32_t*>(bitmap), static_cast<const uint32_t*>(prefix),
+                 nwords, g, reinterpret_cast<int4*>(out_indices), n_out);
   const unsigned grid = static_cast<unsigned>(ceil_div(n_in, kThreads));
-  k_strided_pairs<<<grid, kThreads, 0, stream>>>(
-      reinterpret_cast<const int4*>(indices), n_in, g, bitmap, prefix, n_out, gather_map,
-      scatter_map, overflow, overflow_cap, reinterpret_cast<unsigned long long*>(meta), status);
-  TSC_LAUNCH_CHECK("k_strided_pairs");
+  TSC_LAUNCH_PDL("k_strided_pairs", k_strided_pairs, dim3(grid), dim3(kThreads), 0, stream,
+                 reinterpret_cast<const int4*>(indices), n_in, g, static_cast<const uint32_t*>(bitmap),
+                 static_cast<const uint32_t*>(prefix), n_out, gather_map, scatter_map, overflow, overflow_cap,
+                 reinterpret_cast<unsigned long long*>(meta), status);
   return TSC_OK;
 }
 

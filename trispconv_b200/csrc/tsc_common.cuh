@@ -40,6 +40,52 @@ int check_launch(const char* what);
     if (rc_ != TSC_OK) return rc_;                                           \
   } while (0)
 
+// ---- programmatic dependent launch -------------------------------------------
+// Kernels launched with launch_pdl may be scheduled while the previous kernel
+// of the stream is still running, which hides the launch gap between
+// dependent kernels.  Every kernel that launch_pdl starts calls pdl_wait()
+// before it touches global memory (it then sees everything the previous grid
+// wrote, and that grid has finished reading) and pdl_trigger() to let the next
+// kernel be scheduled once all of its own CTAs have started.  Both are no-ops
+// for a kernel launched the ordinary way.  TRISPCONV_B200_PDL=0 turns the
+// attribute off (ordinary launches).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// Launches through launch_pdl and checks the result like TSC_LAUNCH_CHECK.
+#define TSC_LAUNCH_PDL(what, kern, grid, block, smem, stream, ...)                   \
+  do {                                                                              \
+    cudaError_t e_ = ::tsc::launch_pdl(kern, grid, block, smem, stream, __VA_ARGS__); \
+    if (e_ != cudaSuccess) {                                                        \
+      ::tsc::set_error("launch of %s failed: %s", what, cudaGetErrorString(e_));    \
+      return TSC_ERR_CUDA;                                                          \
+    }                                                                               \
+    TSC_LAUNCH_CHECK(what);                                                         \
+  } while (0)
+
+// Fills n1 32-bit words at p1 with v1 and n2 words at p2 with v2 (p2 may be
+// NULL) in one PDL launch: the stream's memsets of the hot path, as a kernel
+// that joins the dependent-launch chain.
+int fill_words(void* p1, uint32_t v1, int64_t n1, void* p2, uint32_t v2, int64_t n2, cudaStream_t stream);
+
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
 }

@@ -14,6 +14,7 @@ synchronisation; a strided map synchronises once to learn its output count.
 """
 from __future__ import annotations
 
+import os
 import weakref
 from typing import List, Optional, Sequence, Tuple
 
@@ -237,6 +238,22 @@ def _eager_check(device: torch.device) -> None:
         L.check_device_status(device)
 
 
+# Grids of at most DENSE_MAX_CELLS cells (batch * D * H * W) are mapped through
+# a direct-address int32 table (tsc_subm_kmap_dense) that stays allocated per
+# device and stream and holds -1 between calls; larger grids use the hash.
+DENSE_MAX_CELLS = int(os.environ.get("TRISPCONV_B200_DENSE_MAX_CELLS", str(1 << 28)))
+_dense_tables: dict = {}
+
+
+def _dense_table(dev: torch.device, stream: int, cells: int) -> torch.Tensor:
+    key = (dev.index, stream)
+    t = _dense_tables.get(key)
+    if t is None or t.numel() < cells:
+        t = torch.full((cells,), -1, dtype=torch.int32, device=dev)
+        _dense_tables[key] = t
+    return t
+
+
 def generate_subm_indice_pairs(indices: torch.Tensor, spatial_shape, batch_size: int, kernel_size,
                                dilation=1) -> IndiceData:
     """Submanifold kernel map (indices.py:67-140): output set == input set."""
@@ -251,11 +268,19 @@ def generate_subm_indice_pairs(indices: torch.Tensor, spatial_shape, batch_size:
     geo = L.make_geometry(batch_size, shape, shape, ks, (1, 1, 1), (0, 0, 0), dl)
     gather = torch.empty((K, n), dtype=torch.int32, device=dev)
     meta = torch.empty(L.META_COUNTS + K, dtype=torch.int64, device=dev)
-    ws = L.workspace(lib.tsc_subm_kmap_workspace(n), dev)
+    cells = int(batch_size) * shape[0] * shape[1] * shape[2]
+    stream = L.stream_ptr(dev)
     with L.on_device(dev):
-        L.check(lib.tsc_subm_kmap(idx.data_ptr(), n, L.byref(geo), ws.data_ptr(), ws.numel(),
-                                  gather.data_ptr(), meta.data_ptr(), L.status_word(dev).data_ptr(),
-                                  L.stream_ptr(dev)), "tsc_subm_kmap")
+        if 0 < cells <= DENSE_MAX_CELLS:
+            table = _dense_table(dev, stream, cells)
+            L.check(lib.tsc_subm_kmap_dense(idx.data_ptr(), n, L.byref(geo), table.data_ptr(), table.numel(),
+                                            gather.data_ptr(), meta.data_ptr(), L.status_word(dev).data_ptr(),
+                                            stream), "tsc_subm_kmap_dense")
+        else:
+            ws = L.workspace(lib.tsc_subm_kmap_workspace(n), dev)
+            L.check(lib.tsc_subm_kmap(idx.data_ptr(), n, L.byref(geo), ws.data_ptr(), ws.numel(),
+                                      gather.data_ptr(), meta.data_ptr(), L.status_word(dev).data_ptr(),
+                                      stream), "tsc_subm_kmap")
     _eager_check(dev)
     km = KernelMap(K, n, n, gather, meta, dev, pair_map=gather, pair_mode=0)
     return IndiceData(out_indices=indices, input_indices=indices, input_spatial_shape=spatial_shape,
