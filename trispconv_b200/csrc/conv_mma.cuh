@@ -161,32 +161,54 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
   const int steps = s_misc[0] * n_chunks;
 
   // ---- producer: cp.async one (k, channel chunk) step into a stage --------
+  // Each thread copies the same UA feature units and UB weight units in every
+  // step; their rows, channels and swizzled destinations are fixed per thread
+  // and computed once here, so a step only looks up the gather row.
+  constexpr int UA = BM * UPR / NT;
+  constexpr int UB = (TN * UPR + NT - 1) / NT;
+  static_assert(BM * UPR % NT == 0, "feature copy units per thread");
+  int a_row[UA], a_ch[UA], a_dst[UA];
+#pragma unroll
+  for (int i = 0; i < UA; ++i) {
+    const int u = tid + i * NT;
+    const int r = u / UPR;
+    const int q = u - r * UPR;
+    const int byte = q * CH;
+    a_row[i] = r;
+    a_ch[i] = q * (CH / 2);
+    a_dst[i] = r * (KC * 2) + (swz<KC>(r, byte >> 4) << 4) + (byte & 15);
+  }
+  int b_n[UB], b_ch[UB], b_dst[UB];
+#pragma unroll
+  for (int i = 0; i < UB; ++i) {
+    const int u = tid + i * NT;
+    const int nn = u / UPR;
+    const int q = u - nn * UPR;
+    const int byte = q * CH;
+    b_n[i] = u < TN * UPR ? n0 + nn : -1;
+    b_ch[i] = q * (CH / 2);
+    b_dst[i] = nn * (KC * 2) + (swz<KC>(nn, byte >> 4) << 4) + (byte & 15);
+  }
   auto load_stage = [&](int s, int buf) {
     const int k = s_klist[s / n_chunks];
     const int c0 = (s % n_chunks) * KC;
     unsigned char* sa = smem + buf * C::STAGE;
     unsigned char* sb = sa + C::A_BYTES;
-    for (int u = tid; u < BM * UPR; u += NT) {
-      const int r = u / UPR;
-      const int q = u - r * UPR;
-      const int c = c0 + q * (CH / 2);
-      const int j = s_rows[k * BM + r];
+    const int32_t* rows_k = s_rows + k * BM;
+#pragma unroll
+    for (int i = 0; i < UA; ++i) {
+      const int c = c0 + a_ch[i];
+      const int j = rows_k[a_row[i]];
       const bool valid = j >= 0 && c < c_in;
-      const int byte = q * CH;
-      unsigned char* dst = sa + r * (KC * 2) + (swz<KC>(r, byte >> 4) << 4) + (byte & 15);
-      const T* src = valid ? F + static_cast<int64_t>(j) * c_in + c : F;
-      cp_async<CH>(dst, src, valid);
+      cp_async<CH>(sa + a_dst[i], valid ? F + static_cast<int64_t>(j) * c_in + c : F, valid);
     }
-    for (int u = tid; u < TN * UPR; u += NT) {
-      const int nn = u / UPR;
-      const int q = u - nn * UPR;
-      const int c = c0 + q * (CH / 2);
-      const int n = n0 + nn;
+#pragma unroll
+    for (int i = 0; i < UB; ++i) {
+      if (b_n[i] < 0) continue;
+      const int c = c0 + b_ch[i];
+      const int n = b_n[i];
       const bool valid = n < c_out && c < c_in;
-      const int byte = q * CH;
-      unsigned char* dst = sb + nn * (KC * 2) + (swz<KC>(nn, byte >> 4) << 4) + (byte & 15);
-      const T* src = valid ? W + (static_cast<int64_t>(n) * K + k) * c_in + c : W;
-      cp_async<CH>(dst, src, valid);
+      cp_async<CH>(sb + b_dst[i], valid ? W + (static_cast<int64_t>(n) * K + k) * c_in + c : W, valid);
     }
   };
 
@@ -381,6 +403,21 @@ k_conv_mmaw(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict
   const int wm = warp / WN;
   const int wn = warp % WN;
 
+  // feature copy units of this thread (fixed across steps and tiles)
+  constexpr int UA = BM * UPR / NT;
+  static_assert(BM * UPR % NT == 0, "feature copy units per thread");
+  int a_row[UA], a_ch[UA], a_dst[UA];
+#pragma unroll
+  for (int i = 0; i < UA; ++i) {
+    const int u = tid + i * NT;
+    const int r = u / UPR;
+    const int q = u - r * UPR;
+    const int byte = q * CH;
+    a_row[i] = r;
+    a_ch[i] = q * (CH / 2);
+    a_dst[i] = r * (KC * 2) + (swz<KC>(r, byte >> 4) << 4) + (byte & 15);
+  }
+
   for (int64_t tile = blockIdx.x; tile < n_row_tiles; tile += gridDim.x) {
     const int64_t tile0 = tile * BM;
     // ---- the tile's output rows and gather-map slice -------------------------
@@ -418,16 +455,12 @@ k_conv_mmaw(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict
     auto load_stage = [&](int s, int buf) {
       const int k = s_klist[s];
       unsigned char* sa = smem + buf * C::A_BYTES;
-      for (int u = tid; u < BM * UPR; u += NT) {
-        const int r = u / UPR;
-        const int q = u - r * UPR;
-        const int c = q * (CH / 2);
-        const int j = s_rows[k * BM + r];
-        const bool valid = j >= 0 && c < c_in;
-        const int byte = q * CH;
-        unsigned char* dst = sa + r * (KC * 2) + (swz<KC>(r, byte >> 4) << 4) + (byte & 15);
-        const T* src = valid ? F + static_cast<int64_t>(j) * c_in + c : F;
-        cp_async<CH>(dst, src, valid);
+      const int32_t* rows_k = s_rows + k * BM;
+#pragma unroll
+      for (int i = 0; i < UA; ++i) {
+        const int j = rows_k[a_row[i]];
+        const bool valid = j >= 0 && a_ch[i] < c_in;
+        cp_async<CH>(sa + a_dst[i], valid ? F + static_cast<int64_t>(j) * c_in + a_ch[i] : F, valid);
       }
     };
 
