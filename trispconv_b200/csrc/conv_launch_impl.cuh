@@ -53,6 +53,26 @@ int launch_mmaw_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bia
   return TSC_OK;
 }
 
+// Streamed-weight mma.sync kernel with RB output rows per CTA.
+template <typename T, int TN, int KC, int CH, int RB>
+int launch_mma_rows(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
+                    const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
+                    const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+  using C = mma::Cfg<TN, KC, RB>;
+  auto kern = mma::k_conv_mma<T, TN, KC, CH, RB>;
+  static unsigned long long configured = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL));
+    configured |= 1ull << (dev & 63);
+  }
+  dim3 grid(static_cast<unsigned>(ceil_div(n_out, RB)), static_cast<unsigned>(ceil_div(c_out, TN)));
+  TSC_LAUNCH_PDL("k_conv_mma", kern, grid, dim3(mma::NT), C::bytes(K), stream, f, n_in, c_in, w, bias, gmap, perm,
+                 K, n_out, c_out, ovf, ovf_cap, meta, out, flags, status);
+  return TSC_OK;
+}
+
 template <typename T, int TN, int KC, int CH>
 int launch_mma_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                    const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
@@ -61,19 +81,17 @@ int launch_mma_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias
       static_cast<int64_t>(K) * TN * KC * 2 <= mma::kMaxResidentWeightBytes)
     return launch_mmaw_cfg<T, TN, KC, CH>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
                                           out, flags, status, stream);
-  using C = mma::Cfg<TN, KC>;
-  auto kern = mma::k_conv_mma<T, TN, KC, CH>;
-  static unsigned long long configured = 0;  // one bit per device
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
-    TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL));
-    configured |= 1ull << (dev & 63);
+  // 16-channel chunks with narrow column tiles take 2 * BM rows per CTA (each
+  // weight slice then serves twice the rows).  Measured on the config-3 maps:
+  // 16->32 71.0 -> 68.5 us; 32-channel layers got slower (32->32 102 -> 113
+  // us, 32->64 123 -> 132 us) because the larger tile halves the CTAs per SM.
+  if constexpr (KC == 16 && TN <= 32) {
+    if (n_out >= 4096)
+      return launch_mma_rows<T, TN, KC, CH, 2 * mma::BM>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf,
+                                                         ovf_cap, meta, out, flags, status, stream);
   }
-  dim3 grid(static_cast<unsigned>(ceil_div(n_out, mma::BM)), static_cast<unsigned>(ceil_div(c_out, TN)));
-  TSC_LAUNCH_PDL("k_conv_mma", kern, grid, dim3(mma::NT), C::bytes(K), stream, f, n_in, c_in, w, bias, gmap, perm,
-                 K, n_out, c_out, ovf, ovf_cap, meta, out, flags, status);
-  return TSC_OK;
+  return launch_mma_rows<T, TN, KC, CH, mma::BM>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap,
+                                                 meta, out, flags, status, stream);
 }
 
 // ---- tcgen05 path ------------------------------------------------------------

@@ -24,18 +24,20 @@ constexpr int NT = 256;
 constexpr int NS = 4;
 constexpr int KMAX = 64;  // kernel volumes handled by this path
 
-template <int TN, int KC>
+// RB output rows per CTA (BM, or 2*BM to share each weight slice between
+// more rows).
+template <int TN, int KC, int RB = BM>
 struct Cfg {
-  static constexpr int A_BYTES = BM * KC * 2;
+  static constexpr int A_BYTES = RB * KC * 2;
   static constexpr int B_BYTES = TN * KC * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int PIPE = NS * STAGE;
   static constexpr int OUT_LD = TN + 8;  // fp32 epilogue row stride
-  static constexpr int EPI = BM * OUT_LD * 4;
+  static constexpr int EPI = RB * OUT_LD * 4;
   static constexpr int MAIN = PIPE > EPI ? PIPE : EPI;
-  // rows [K][BM] int32 + out rows [BM] + active list [KMAX] + misc[8]
-  static constexpr int TOTAL = MAIN + (KMAX * BM + BM + KMAX + 8) * 4;  // K = KMAX upper bound
-  static constexpr int bytes(int K) { return MAIN + (K * BM + BM + KMAX + 8) * 4; }
+  // rows [K][RB] int32 + out rows [RB] + active list [KMAX] + misc[8]
+  static constexpr int TOTAL = MAIN + (KMAX * RB + RB + KMAX + 8) * 4;  // K = KMAX upper bound
+  static constexpr int bytes(int K) { return MAIN + (K * RB + RB + KMAX + 8) * 4; }
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -97,7 +99,7 @@ __device__ __forceinline__ int swz(int row, int chunk) {
   return chunk ^ ((row / (8 / C)) % C);
 }
 
-template <typename T, int TN, int KC, int CH>
+template <typename T, int TN, int KC, int CH, int RB = BM>
 __global__ void __launch_bounds__(NT)
 k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__ W,
            const T* __restrict__ bias, const int32_t* __restrict__ gmap, const int32_t* __restrict__ perm,
@@ -105,10 +107,11 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
            const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status) {
   pdl_wait();
   pdl_trigger();
-  using C = Cfg<TN, KC>;
+  using C = Cfg<TN, KC, RB>;
+  static_assert(RB <= NT && RB % BM == 0, "rows per CTA");
   constexpr int WN = (TN == 128) ? 2 : 1;
   constexpr int WM = 8 / WN;
-  constexpr int WTM = BM / WM;
+  constexpr int WTM = RB / WM;
   constexpr int WTN = TN / WN;
   constexpr int MF = WTM / 16;
   constexpr int NF = WTN / 8;
@@ -116,27 +119,27 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
   static_assert(NF % 2 == 0, "B fragments are loaded in pairs");
 
   extern __shared__ __align__(128) unsigned char smem[];
-  int32_t* s_rows = reinterpret_cast<int32_t*>(smem + C::MAIN);  // [K][BM]
-  int32_t* s_orow = s_rows + K * BM;                              // [BM] output row ids (-1 = none)
-  int32_t* s_klist = s_orow + BM;                                 // active offsets
+  int32_t* s_rows = reinterpret_cast<int32_t*>(smem + C::MAIN);  // [K][RB]
+  int32_t* s_orow = s_rows + K * RB;                              // [RB] output row ids (-1 = none)
+  int32_t* s_klist = s_orow + RB;                                 // active offsets
   int32_t* s_misc = s_klist + KMAX;                               // [0] n_active, [1] hit row
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int64_t tile0 = static_cast<int64_t>(blockIdx.x) * BM;
+  const int64_t tile0 = static_cast<int64_t>(blockIdx.x) * RB;
   const int n0 = blockIdx.y * TN;
 
   // ---- stage the tile's output rows and gather-map slice ------------------
   if (tid < KMAX) s_klist[tid] = 0;  // used as per-offset "any pair" flags first
-  if (tid < BM) {
+  if (tid < RB) {
     const int64_t t = tile0 + tid;
     s_orow[tid] = t < n_out ? (perm != nullptr ? __ldg(&perm[t]) : static_cast<int32_t>(t)) : -1;
   }
   __syncthreads();
-  for (int e = tid; e < K * BM; e += NT) {
-    const int k = e / BM;
-    const int r = e - k * BM;
+  for (int e = tid; e < K * RB; e += NT) {
+    const int k = e / RB;
+    const int r = e - k * RB;
     const int o = s_orow[r];
     int j = -1;
     if (o >= 0) {
@@ -164,9 +167,9 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
   // Each thread copies the same UA feature units and UB weight units in every
   // step; their rows, channels and swizzled destinations are fixed per thread
   // and computed once here, so a step only looks up the gather row.
-  constexpr int UA = BM * UPR / NT;
+  constexpr int UA = RB * UPR / NT;
   constexpr int UB = (TN * UPR + NT - 1) / NT;
-  static_assert(BM * UPR % NT == 0, "feature copy units per thread");
+  static_assert(RB * UPR % NT == 0, "feature copy units per thread");
   int a_row[UA], a_ch[UA], a_dst[UA];
 #pragma unroll
   for (int i = 0; i < UA; ++i) {
@@ -194,7 +197,7 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
     const int c0 = (s % n_chunks) * KC;
     unsigned char* sa = smem + buf * C::STAGE;
     unsigned char* sb = sa + C::A_BYTES;
-    const int32_t* rows_k = s_rows + k * BM;
+    const int32_t* rows_k = s_rows + k * RB;
 #pragma unroll
     for (int i = 0; i < UA; ++i) {
       const int c = c0 + a_ch[i];
@@ -288,7 +291,7 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
       const int j = __ldg(&ovf[3 * e + 2]);
       if (tid == 0) s_misc[1] = -1;
       __syncthreads();
-      if (tid < BM && s_orow[tid] == o) s_misc[1] = tid;
+      if (tid < RB && s_orow[tid] == o) s_misc[1] = tid;
       __syncthreads();
       const int r = s_misc[1];
       if (r >= 0 && k >= 0 && k < K && j >= 0 && j < n_in && tid < TN && n0 + tid < c_out) {
@@ -304,7 +307,7 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
 
   const bool relu = (flags & TSC_CONV_RELU) != 0;
   constexpr int CPR_OUT = TN / 8;  // 16-byte output chunks per row
-  for (int u = tid; u < BM * CPR_OUT; u += NT) {
+  for (int u = tid; u < RB * CPR_OUT; u += NT) {
     const int r = u / CPR_OUT;
     const int q = u - r * CPR_OUT;
     const int o = s_orow[r];
