@@ -27,8 +27,10 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
+from typing import Optional
 
 import numpy as np
 
@@ -62,10 +64,78 @@ def dist_env():
     return ws, rank, local
 
 
-def workload_for_rank(rank: int, batch: int = 4):
+class BenchWorkload:
+    """One rank's share of a benchmark workload.
+
+    indices: (N, 4) int32 [b, z, y, x] with GLOBAL batch ids; features: host
+    array (config 3) or None when the features are drawn on the device
+    (config 5: 8 M x 256 normals would take minutes on the host);
+    layers: the layer list the network is built from."""
+
+    def __init__(self, name, indices, features, spatial_shape, batch_size, layers, scaling, samples,
+                 total_voxels, info):
+        self.name = name
+        self.indices = indices
+        self.features = features
+        self.spatial_shape = list(spatial_shape)
+        self.batch_size = batch_size
+        self.layers = layers
+        self.scaling = scaling
+        self.samples = samples          # [b0, b1) of this rank
+        self.total_voxels = total_voxels  # voxels of one step over ALL ranks
+        self.info = info
+
+    @property
+    def n_voxels(self) -> int:
+        return len(self.indices)
+
+
+def _c5_coords(b: int) -> np.ndarray:
     from trispconv_b200.testing import synthetic as syn
 
-    return syn.config3(seed=3 + 1000 * rank, batch=batch)
+    return syn.config5_sample_coords(b)
+
+
+def config5_coords(b0: int, b1: int) -> np.ndarray:
+    """Config-5 coordinates of samples [b0, b1) (global batch ids), one
+    worker process per sample.  The pool uses `spawn` and starts before this
+    process touches the GPU."""
+    import multiprocessing as mp
+
+    from trispconv_b200.testing import synthetic as syn
+
+    bs = list(range(b0, b1))
+    if not bs:
+        return np.zeros((0, 4), np.int32)
+    workers = max(1, min(len(bs), (os.cpu_count() or 2) // 2))
+    if workers > 1:
+        with mp.get_context("spawn").Pool(workers) as pool:
+            zyx = pool.map(_c5_coords, bs)
+    else:
+        zyx = [_c5_coords(b) for b in bs]
+    rows = [np.concatenate([np.full((len(p), 1), b, np.int64), p.astype(np.int64)], 1) for b, p in zip(bs, zyx)]
+    return np.ascontiguousarray(np.concatenate(rows).astype(np.int32))
+
+
+def make_workload(args, rank: int, ws: int) -> BenchWorkload:
+    """config3: every rank runs its own batch of 4 (weak scaling).
+    config5: ONE batch of 16 split by sample over the ranks (strong
+    scaling), a single SubMConv3d(C, C, 3) without bias."""
+    from trispconv_b200 import shard
+    from trispconv_b200.testing import synthetic as syn
+
+    if args.workload == "config3":
+        wl = syn.config3(seed=3 + 1000 * rank, batch=4)
+        return BenchWorkload(WORKLOAD, wl.indices, wl.features, wl.spatial_shape, wl.batch_size, wl.layers,
+                             "weak", (0, wl.batch_size), ws * wl.n_voxels,
+                             {"layers": 12, "box_voxels": wl.info.get("box_voxels")})
+    c = args.channels
+    b0, b1 = shard.batch_range(16, rank, ws)
+    idx = config5_coords(b0, b1)
+    rng = np.random.default_rng(5)
+    layers = syn.init_layers([syn.layer("subm", c, c, 3, key="subm")], rng, np.float16, bias_std=None)
+    return BenchWorkload(f"config5_subm3_c{c}_fp16", idx, None, (64, 512, 512), 16, layers, "strong", (b0, b1),
+                         16 * 500_000, {"layers": 1, "channels": c})
 
 
 # --------------------------------------------------------------------------
@@ -73,40 +143,86 @@ def workload_for_rank(rank: int, batch: int = 4):
 # --------------------------------------------------------------------------
 
 
-def cpu_forward_time(wl, reps: int = 1) -> float:
+def _host_features(wl: BenchWorkload, n_rows: Optional[int] = None) -> np.ndarray:
+    if wl.features is not None:
+        return wl.features if n_rows is None else wl.features[:n_rows]
+    c = wl.layers[0]["cin"]
+    n = wl.n_voxels if n_rows is None else n_rows
+    return np.random.default_rng(55).standard_normal((n, c), dtype=np.float32).astype(np.float16)
+
+
+def cpu_forward_time(indices, features, spatial_shape, batch_size, layers) -> float:
+    """One forward of `layers` through the numpy port of the reference's CPU
+    path in fp32, with the reference's dense B*D*H*W key table."""
     import oracle
+    from oracle import indices as OI
 
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        oracle.run_layers(wl.indices, wl.features, wl.spatial_shape, wl.batch_size, wl.layers)
-    return (time.perf_counter() - t0) / reps
+    OI.set_table_kind("dense")
+    try:
+        t0 = time.perf_counter()
+        oracle.run_layers(indices, features, spatial_shape, batch_size, layers)
+        return time.perf_counter() - t0
+    finally:
+        OI.set_table_kind("sorted")
 
 
-def cpu_baseline(wl) -> dict:
-    secs = cpu_forward_time(wl)
-    return {"value": wl.n_voxels / secs, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-            "sample": f"one full forward of the config-3 batch ({wl.batch_size} samples, {wl.n_voxels} voxels), "
-                      f"numpy oracle in fp32, {secs:.2f} s"}
+def cpu_sample(wl: BenchWorkload):
+    """(indices, features, batch_size, description) of the bounded CPU sample:
+    the whole config-3 batch; one config-5 sample (500k voxels)."""
+    if wl.scaling == "weak":
+        return (wl.indices, _host_features(wl), wl.batch_size,
+                f"one full forward of the config-3 batch ({wl.batch_size} samples, {wl.n_voxels} voxels)")
+    b0 = wl.samples[0]
+    m = wl.indices[:, 0] == b0
+    idx = np.ascontiguousarray(wl.indices[m])
+    idx[:, 0] = 0
+    return (idx, _host_features(wl, len(idx)), 1,
+            f"one config-5 sample ({len(idx)} voxels, C={wl.layers[0]['cin']}) of the batch of 16")
+
+
+def cpu_baseline(wl: BenchWorkload) -> dict:
+    idx, feats, batch, what = cpu_sample(wl)
+    secs = cpu_forward_time(idx, feats, wl.spatial_shape, batch, wl.layers)
+    return {"value": len(idx) / secs, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{what}: numpy port of the reference's CPU path in fp32 with its dense B*D*H*W key "
+                      f"table, {secs:.2f} s"}
 
 
 def run_reference(args) -> None:
+    """The reference's CPU path (numpy port, fp32, the reference's dense key
+    table) on the GPU arm's config: each step is one forward of the
+    config-3 batch of 4 (config 5: one sample of the batch of 16).  Under
+    torchrun rank 0 alone runs; the other ranks exit without work."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
-    wl = workload_for_rank(0).sample_slice(0, 1)  # bounded sample: one 40k-voxel cloud per step
+    # config 5: only sample 0 is generated (the bounded sample of a step)
+    wl = make_workload(args, 0, 16 if args.workload == "config5" else 1)
+    idx, feats, batch, what = cpu_sample(wl)
+    torch_threads = None
+    try:
+        import torch
+
+        torch_threads = torch.get_num_threads()
+    except ImportError:
+        pass
     for _ in range(args.warmup):
-        cpu_forward_time(wl)
-    times = [cpu_forward_time(wl) for _ in range(args.steps)]
+        cpu_forward_time(idx, feats, wl.spatial_shape, batch, wl.layers)
+    times = [cpu_forward_time(idx, feats, wl.spatial_shape, batch, wl.layers) for _ in range(args.steps)]
     secs = float(np.mean(times))
-    value = wl.n_voxels / secs
+    value = len(idx) / secs
+    same = wl.scaling == "weak"
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "batch": wl.batch_size, "voxels": wl.n_voxels,
-                       "spatial_shape": wl.spatial_shape, "layers": 12, "device": "cpu"},
+            "scaling": wl.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl.name, "batch": batch, "voxels": len(idx),
+                       "spatial_shape": wl.spatial_shape, "layers": wl.info["layers"], "device": "cpu",
+                       "same_config": same},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"{args.steps} forwards of one config-3 sample ({wl.n_voxels} voxels) "
-                                       "through the numpy port of the reference's CPU path, fp32"},
+                             "torch_threads": torch_threads,
+                             "sample": f"{args.steps} steps, each {what}, through the numpy port of the "
+                                       "reference's CPU path (fp32, the reference's dense B*D*H*W int64 key "
+                                       "table), numpy/BLAS on all host threads"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -121,14 +237,16 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, keep: Optional[str] = None):
+        """Samples go to a temporary file; `keep` (--clock-log) names a file
+        that receives a copy of the raw samples when sampling stops."""
         self.gpu = gpu_index
         self.proc = None
-        self.out = ROOT / "gpurun_out" / f"clocks_bench_{gpu_index}_{os.getpid()}.csv"
+        self.keep = keep
+        self.out = Path(tempfile.gettempdir()) / f"trispconv_b200_clocks_{gpu_index}_{os.getpid()}.csv"
 
     def start(self):
         try:
-            self.out.parent.mkdir(exist_ok=True)
             self.fh = open(self.out, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -142,9 +260,16 @@ class ClockSampler:
         self.proc.terminate()
         self.proc.wait(timeout=10)
         self.fh.close()
+        text = self.out.read_text()
+        try:
+            self.out.unlink()
+        except OSError:
+            pass
+        if self.keep:
+            Path(self.keep).write_text(text)
         sm, smax, reasons = [], [], set()
         names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.out.read_text().splitlines():
+        for line in text.splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -316,11 +441,16 @@ def run_ours(args) -> None:
     from trispconv_b200.testing import networks
 
     peaks = load_peaks()
-    wl = workload_for_rank(rank)
+    wl = make_workload(args, rank, ws)
     net = networks.build_network(wl.layers, dev, torch.float16)
-    feats_d = torch.from_numpy(wl.features).to(dev)
     idx_d = torch.from_numpy(wl.indices).to(dev)
-    feats_h = torch.from_numpy(wl.features).pin_memory()
+    if wl.features is not None:
+        feats_d = torch.from_numpy(wl.features).to(dev)
+    else:  # N(0, 1) features drawn on the device, seeded per rank
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(55 + rank)
+        feats_d = torch.randn((wl.n_voxels, wl.layers[0]["cin"]), generator=gen, device=dev).half()
+    feats_h = feats_d.cpu().pin_memory()
     idx_h = torch.from_numpy(wl.indices).pin_memory()
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     probe = ConvProbe()
@@ -336,7 +466,7 @@ def run_ours(args) -> None:
 
     # nvidia-smi samples every 200 ms from the first warm-up step to the end of
     # the timed region (a short timed region alone may see a single sample).
-    clocks = ClockSampler(torch.cuda.current_device())
+    clocks = ClockSampler(torch.cuda.current_device(), args.clock_log)
     clocks.start()
     # warm-up with the probe on, so that the allocator reaches the timed
     # loop's steady state; the warm-up records are dropped
@@ -382,7 +512,12 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
-    value = ws * wl.n_voxels / (ms_per_step / 1e3)
+    # voxels of one step over all ranks (each rank's own count, summed)
+    nv = torch.tensor([wl.n_voxels], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(nv, op=dist.ReduceOp.SUM)
+    step_voxels = float(nv.item())
+    value = step_voxels / (ms_per_step / 1e3)
     _lib.check_device_status(dev)
 
     rows = layer_table(probe.records, peaks, per_step)
@@ -415,6 +550,11 @@ def run_ours(args) -> None:
         roof = {"bound": "tensor", "achieved": dom_flops / n_dom / (dom_ms / n_dom / 1e3) / 1e12,
                 "peak": peaks["bf16_tflops"], "unit": "TFLOP/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
+    if roof["bound"] == "tensor":
+        # the same launches against the cuBLAS figure measured back to back
+        # for seconds under the power cap
+        roof["peak_sustained"] = peaks["bf16_tflops_sustained"]
+        roof["frac_sustained"] = roof["achieved"] / peaks["bf16_tflops_sustained"]
     roof["traffic"] = measured_traffic(dom, dom_bytes / n_dom)
     roof["traffic_note"] = ("ncu DRAM read+write of one captured launch (profiles/traffic.json), scaled by "
                             "algorithmic bytes to the average launch")
@@ -464,7 +604,7 @@ def run_ours(args) -> None:
     t_sync = torch.tensor([e2e_ms / e2e_steps], dtype=torch.float64, device=dev)
     if ws > 1:
         dist.all_reduce(t_sync, op=dist.ReduceOp.MAX)
-    e2e_sync_value = ws * wl.n_voxels / (float(t_sync.item()) / 1e3)
+    e2e_sync_value = step_voxels / (float(t_sync.item()) / 1e3)
 
     # Streamed: a serving loop.  Step i's inputs go up on an upload stream and
     # its output features come back on a download stream, so the copies of
@@ -518,7 +658,32 @@ def run_ours(args) -> None:
     t = torch.tensor([s_start.elapsed_time(s_end) / e2e_steps], dtype=torch.float64, device=dev)
     if ws > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = ws * wl.n_voxels / (float(t.item()) / 1e3)
+    e2e_value = step_voxels / (float(t.item()) / 1e3)
+
+    # ---- output gather (N > 1): the one collective of the sharded path -----
+    gather = None
+    if ws > 1:
+        from trispconv_b200 import shard
+
+        yk = forward_resident()
+        g_ms = []
+        for i in range(4):  # first call untimed (NCCL channel set-up)
+            barrier()
+            g0 = torch.cuda.Event(enable_timing=True)
+            g1 = torch.cuda.Event(enable_timing=True)
+            g0.record()
+            gi, gf = shard.gather_sparse(yk.indices, yk.features)
+            g1.record()
+            g1.synchronize()
+            if i:
+                g_ms.append(g0.elapsed_time(g1))
+        tg = torch.tensor([float(np.mean(g_ms))], dtype=torch.float64, device=dev)
+        dist.all_reduce(tg, op=dist.ReduceOp.MAX)
+        gather = {"ms": float(tg.item()), "rows": int(gi.shape[0]),
+                  "bytes_per_rank": int(gf.numel() * gf.element_size() + gi.numel() * gi.element_size()),
+                  "what": "shard.gather_sparse: NCCL all-gather of row counts, then of the padded output "
+                          "indices and features, to every rank (max over ranks, outside the timed steps)"}
+        del gi, gf, yk
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -527,10 +692,12 @@ def run_ours(args) -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": wl.scaling,
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "batch_per_gpu": wl.batch_size, "voxels_per_gpu": wl.n_voxels,
-                       "spatial_shape": wl.spatial_shape, "layers": 12, "parallelism": f"batch-shard x{ws}",
+            "config": {"workload": wl.name, "batch": wl.batch_size if wl.scaling == "strong" else ws * wl.batch_size,
+                       "samples_per_gpu": wl.samples[1] - wl.samples[0], "voxels_per_gpu": wl.n_voxels,
+                       "voxels_per_step": step_voxels, "spatial_shape": wl.spatial_shape,
+                       "layers": wl.info["layers"], "parallelism": f"batch-shard x{ws}",
                        "l2": "flushed between steps (256 MiB write outside the timed events)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": float(t.item()), "steps": e2e_steps, "compute_step_ms": s_step_ms,
@@ -544,6 +711,7 @@ def run_ours(args) -> None:
             "gpu_launches": launches,
             "roofline": roof,
             "cpu_baseline": cpu,
+            "gather": gather,
             "clocks": clk,
             "wall_s_timed_region": wall,
             "step_ms": [round(v, 4) for v in step_ms],
@@ -561,6 +729,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="config3", choices=["config3", "config5"],
+                    help="config3: SECOND backbone, batch 4 per GPU (weak scaling, the headline metric); "
+                         "config5: SubMConv3d C->C on one batch of 16 x 500k voxels split over the GPUs "
+                         "(strong scaling)")
+    ap.add_argument("--channels", type=int, default=256, choices=[64, 128, 256], help="config5 channels")
+    ap.add_argument("--clock-log", default=None, help="file that receives the raw nvidia-smi clock samples")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

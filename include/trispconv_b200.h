@@ -71,6 +71,10 @@ extern "C" {
 #define TSC_CONV_USE_TC     0x200  /* use the tcgen05 (TMEM) kernel where it applies */
 #define TSC_CONV_TC_SIMPLE  0x400  /* testing: one-tile-per-CTA tcgen05 kernel instead of the persistent one */
 #define TSC_CONV_NO_RESIDENT_W 0x800  /* testing: mma.sync kernel without resident weights */
+#define TSC_CONV_TEST_WAIT_TIMEOUT 0x1000  /* testing: the persistent tcgen05 kernel computes nothing; one
+                                              thread waits on a barrier nothing arrives at with a ~0.1 ms
+                                              limit, which runs out and sets TSC_STATUS_WAIT_TIMEOUT (the
+                                              output is left unwritten) */
 
 /* Weight layouts accepted by tsc_conv_forward. */
 #define TSC_W_KCC  0  /* (K, C_in, C_out): the reference's internal layout (weight.py:36) */
@@ -313,6 +317,11 @@ TSC_API int tsc_row_order(const int32_t* gather_map, int32_t k_vol, int64_t n_ou
  *     inputs fail with TSC_ERR_WORKSPACE and a message naming the limit.
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - The current device must be the one that owns `stream` (the array's
+ *     address is per device); otherwise the call returns
+ *     TSC_ERR_UNSUPPORTED.
+ *   - The launches are those of tsc_subm_kmap (one fill kernel for meta and
+ *     the table, then the build and the query).
  *   - All calls on a device share the one array: calls whose work overlaps
  *     on the GPU (different streams, or threads) race and give wrong maps;
  *     serialise them.  Each call clears the part of the table it uses. */

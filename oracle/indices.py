@@ -1,10 +1,12 @@
 """Numpy restatement of the reference's indice-pair generation.
 
 TEST INFRASTRUCTURE ONLY (see oracle/__init__.py).  Each function cites the
-reference lines it restates.  The one deliberate change: the reference's
-dense B*D*H*W int64 lookup table (indices.py:54-64) is replaced by a sorted
-key array + searchsorted with the same last-write-wins semantics, so the
-oracle also runs on grids whose dense table would not fit in memory.
+reference lines it restates.  One deliberate change by default: the
+reference's dense B*D*H*W int64 lookup table (indices.py:54-64) is replaced
+by a sorted key array + searchsorted with the same last-write-wins
+semantics, so the oracle also runs on grids whose dense table would not fit
+in memory.  set_table_kind("dense") restores the reference's own table (the
+CPU reference arm of bench.py times that one).
 """
 from __future__ import annotations
 
@@ -78,6 +80,36 @@ class _LastWriteTable:
         return np.where(hit, self.rows[pos], -1)
 
 
+class _DenseTable:
+    """indices.py:54-64 (_build_hash_table) as the reference builds it: a
+    B*D*H*W int64 array filled with -1, then ``table[encoded] = arange(N)``.
+    numpy's fancy assignment writes in index order, so the last row of a
+    duplicated coordinate wins, as in the reference (checked against
+    _LastWriteTable by tests/test_oracle_golden.py)."""
+
+    def __init__(self, keys: np.ndarray, cells: int):
+        self.table = np.full(int(cells), -1, dtype=np.int64)
+        self.table[keys] = np.arange(len(keys), dtype=np.int64)
+
+    def lookup(self, q: np.ndarray) -> np.ndarray:
+        return self.table[q]
+
+
+# Key -> row table of subm_pairs: "sorted" (_LastWriteTable, the default: it
+# runs on grids whose dense table would not fit in memory) or "dense" (the
+# reference's own B*D*H*W table, _DenseTable), which bench.py's CPU
+# reference arm times because that table fill is the reference's dominant
+# CPU cost on the large grids.
+TABLE_KIND = "sorted"
+
+
+def set_table_kind(kind: str) -> None:
+    global TABLE_KIND
+    if kind not in ("sorted", "dense"):
+        raise ValueError(kind)
+    TABLE_KIND = kind
+
+
 def _check_in_grid(indices: np.ndarray, spatial_shape, batch_size):
     if len(indices) == 0:
         return
@@ -96,7 +128,11 @@ def subm_pairs(indices: np.ndarray, spatial_shape, batch_size: int, kernel_size,
     D, H, W = (int(v) for v in spatial_shape)
     indices = np.ascontiguousarray(indices, dtype=np.int32)
     _check_in_grid(indices, (D, H, W), batch_size)
-    table = _LastWriteTable(encode_coords(indices, D, H, W))
+    keys = encode_coords(indices, D, H, W)
+    if TABLE_KIND == "dense":
+        table = _DenseTable(keys, int(batch_size) * D * H * W)
+    else:
+        table = _LastWriteTable(keys)
     ib = indices[:, 0].astype(np.int64)
     iz = indices[:, 1].astype(np.int64)
     iy = indices[:, 2].astype(np.int64)

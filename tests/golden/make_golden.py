@@ -216,7 +216,7 @@ def config_digests() -> None:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="checkout of the reference (mrpulford/trispconv)")
     ap.add_argument("--skip-configs", action="store_true")
     args = ap.parse_args()
     ref = Path(args.reference)

@@ -17,8 +17,9 @@ from trispconv_b200 import _lib  # noqa: E402
 
 
 def test_reference_arm_prints_one_contract_line():
-    """--impl reference times the CPU path on one config-3 sample per step
-    and prints one JSON line with the base contract's keys."""
+    """--impl reference times the CPU path on the GPU arm's own config (the
+    config-3 batch of 4 per step, the reference's dense key table) and prints
+    one JSON line with the base contract's keys."""
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
     r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
                         "--warmup", "3"], capture_output=True, text=True, timeout=600, env=env, cwd=ROOT)
@@ -34,6 +35,8 @@ def test_reference_arm_prints_one_contract_line():
     assert d["steps"] == 1 and d["warmup"] == 3 and d["n_gpus"] == 1
     assert d["value"] > 0 and d["ms_per_step"] > 0
     assert d["config"]["workload"] == bench.WORKLOAD
+    assert d["config"]["same_config"] is True and d["config"]["batch"] == 4
+    assert "dense" in d["cpu_baseline"]["sample"]
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["kind"] == "port" and cb["cores"] >= 1 and cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}

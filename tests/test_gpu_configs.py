@@ -3,11 +3,16 @@
 Kernel maps: SHA-256 digests of every layer's pair lists / out_indices,
 compared with the digests recorded from the reference itself
 (tests/golden/ref_digests.json) -- bit-exact at full size.
-Features: against the CPU oracle, fp32 at 1e-4 (configs 1, 2), fp16 at a
-scale-relative 1e-2 against the fp32 oracle (configs 3-5; configs 4 and 5 on
-a subset of samples / output rows to keep the oracle fast).
+Features: against the CPU oracle, fp32 at 1e-4 (configs 1, 2), fp16 within
+rel 1e-2 of the fp32 oracle elementwise (gpu_util.assert_close_rel: configs
+3-5).  Config 4 compares every one of its 8 samples, one oracle run per
+sample, with its slice of the full-batch GPU output.  Config 5 recomputes a
+row subset that changes from run to run (seed printed on failure;
+TRISPCONV_TEST_SEED fixes it) plus the rows at the first, last and a sample
+of interior 256-row tile boundaries.
 """
 import hashlib
+import os
 
 import numpy as np
 import pytest
@@ -66,19 +71,28 @@ def test_config3_second_backbone(cuda):
     assert_close_rel(np_(y.features.float()), ref.features, 1e-2, "SECOND backbone output")
 
 
-def test_config4_unet_kernel_maps(cuda):
+def test_config4_unet_kernel_maps_and_all_samples(cuda):
+    """Full batch of 8 on the GPU: kernel-map digests, then every sample's
+    output slice against its own oracle run (samples are independent; the
+    output is batch-major, so sample b is a contiguous block of rows)."""
     wl = syn.config4()
     y, seen = _run(wl, cuda, torch.float16)
     _check_digests("config4", wl, seen)
-    assert y.features.shape == (wl.n_voxels, 32) and torch.isfinite(y.features).all()
-
-
-def test_config4_unet_features_one_sample(cuda):
-    wl = syn.config4().sample_slice(0, 1)
-    y, _ = _run(wl, cuda, torch.float16)
-    ref = oracle.run_layers(wl.indices, wl.features, wl.spatial_shape, wl.batch_size, wl.layers)
-    assert np.array_equal(np_(y.indices), ref.indices)
-    assert_close_rel(np_(y.features.float()), ref.features, 1e-2, "U-Net output")
+    assert y.features.shape == (wl.n_voxels, 32)
+    got_idx = np_(y.indices)
+    got_f = np_(y.features.float())
+    assert np.all(np.diff(got_idx[:, 0]) >= 0), "output is not batch-major"
+    start = 0
+    for b in range(wl.batch_size):
+        s = wl.sample_slice(b, b + 1)
+        ref = oracle.run_layers(s.indices, s.features, s.spatial_shape, s.batch_size, s.layers)
+        stop = start + len(ref.indices)
+        sl = got_idx[start:stop]
+        assert np.all(sl[:, 0] == b), f"sample {b}: rows {start}:{stop} are not sample {b}"
+        assert np.array_equal(sl[:, 1:], ref.indices[:, 1:]), f"sample {b}: coordinates"
+        assert_close_rel(got_f[start:stop], ref.features, 1e-2, f"U-Net output, sample {b}")
+        start = stop
+    assert start == len(got_idx)
 
 
 def test_config5_kernel_map(cuda):
@@ -102,8 +116,14 @@ def test_config5_features_rows(cuda, channels):
     random 20k-row subset of the outputs from the oracle's own pairs."""
     wl = syn.config5(channels)
     y, seen = _run(wl, cuda, torch.float16)
-    rng = np.random.default_rng(channels)
-    rows = np.sort(rng.choice(wl.n_voxels, 20000, replace=False))
+    seed = int(os.environ.get("TRISPCONV_TEST_SEED", int.from_bytes(os.urandom(4), "little")))
+    rng = np.random.default_rng([seed, channels])
+    n = wl.n_voxels
+    tile = 256  # output rows per tile of the tensor-core kernels
+    starts = rng.choice(np.arange(tile, n - tile, tile), 64, replace=False)
+    edges = np.concatenate([np.arange(tile), np.arange(n - tile, n)] +
+                           [np.arange(s0 - 2, s0 + 2) for s0 in starts])
+    rows = np.unique(np.concatenate([rng.choice(n, 20000, replace=False), edges]))
     spec = wl.layers[0]
     pairs = _config5_pairs(wl)
     w = oracle.normalize_weight(spec["weight"].astype(np.float32), (3, 3, 3), channels, channels)
@@ -116,4 +136,4 @@ def test_config5_features_rows(cuda, channels):
         if sel.any():
             want[pos[pairs.pairs_out[k][sel]]] += f[pairs.pairs_in[k][sel]] @ w[k]
     got = np_(y.features[torch.from_numpy(rows).to(cuda)].float())
-    assert_close_rel(got, want, 1e-2, f"config5 C={channels}")
+    assert_close_rel(got, want, 1e-2, f"config5 C={channels} (TRISPCONV_TEST_SEED={seed})")

@@ -200,7 +200,7 @@ def test_low_precision_vs_fp32_oracle(cuda, dtype, cin, cout):
         assert yt.features.dtype == dtype
         ref = oracle.network.conv_layer(oracle.network.OracleTensor(f.astype(np_dt).astype(np.float32), idx, shape, 1), spec)
         assert np.array_equal(np_(yt.indices), ref.indices)
-        assert_close_rel(np_(yt.features.float()), ref.features, 1e-2, f"{kind} {dtype}")
+        assert_close_rel(np_(yt.features.float()), ref.features, 1e-2, f"{kind} {dtype}", dtype=dtype)
 
 
 def test_sequential_relu_fusion_matches_unfused(cuda, monkeypatch):

@@ -186,3 +186,41 @@ def test_tcp_dynamic_and_round_robin_schedules_agree(cuda):
     torch.cuda.synchronize()
     L.check_device_status(cuda)
     assert torch.equal(outs[0], outs[1])
+
+
+def test_tcp_concurrent_streams_keep_separate_tile_counters(cuda):
+    """Two 64-channel convolutions on the persistent kernel, issued on two
+    streams so that they can run at the same time, each give exactly the
+    single-stream result: every stream has its own tile counter (a shared one
+    would be zeroed by one call while the other's CTAs take tiles from it)."""
+    from trispconv_b200 import _lib as L
+
+    rng = np.random.default_rng(21)
+    shape = (60, 60, 60)
+    m = spconv.SubMConv3d(64, 64, 3, indice_key="s").to(cuda)
+    with torch.no_grad():
+        m.weight.normal_(0, 0.05)
+    m = m.half()
+    xs = []
+    for n in (150_000, 120_000):
+        idx = torch.from_numpy(_cloud(rng, shape, n)).to(cuda)
+        f = torch.from_numpy(rng.standard_normal((n, 64)).astype(np.float32)).to(cuda).half()
+        xs.append(spconv.SparseConvTensor(f, idx, shape, 1))
+    prev = Fn.kernel_flags()
+    Fn.set_tensor_memory_path(True)
+    try:
+        refs = [m(x).features for x in xs]  # builds and caches the maps
+        torch.cuda.synchronize()
+        streams = [torch.cuda.Stream(cuda), torch.cuda.Stream(cuda)]
+        assert L.tile_counter(cuda, streams[0].cuda_stream) is not L.tile_counter(cuda, streams[1].cuda_stream)
+        for _ in range(4):
+            outs = []
+            for s, x in zip(streams, xs):
+                with torch.cuda.stream(s):
+                    outs.append(m(x).features)
+            torch.cuda.synchronize()
+            for o, r in zip(outs, refs):
+                assert torch.equal(o, r)
+    finally:
+        Fn.set_kernel_flags(prev)
+    L.check_device_status(cuda)

@@ -44,20 +44,14 @@ def test_tensor_asserts_int32():
         spconv.SparseConvTensor(torch.randn(3), torch.zeros(3, 4, dtype=torch.int32), [4, 4, 4], 1)
 
 
-def test_dense_host_tensor():
+def test_dense_host_tensor_raises():
+    """dense() runs on the GPU only (tsc_to_dense); CPU tensors are refused
+    like at every other entry point, not scattered on the host."""
     x = make_sparse(B=2, N=10, C=3, D=4, H=5, W=6)
-    idx = x.indices.clone()
-    idx[:, 1] %= 4
-    idx[:5, 0] = 0
-    idx[5:, 0] = 1
-    x2 = spconv.SparseConvTensor(x.features, idx, [4, 5, 6], 2)
-    d = x2.dense()
-    assert d.shape == (2, 3, 4, 5, 6)
-    assert x2.dense(channels_first=False).shape == (2, 4, 5, 6, 3)
-    bad = idx.clone()
-    bad[0, 1] = 9
-    with pytest.raises(AssertionError):
-        spconv.SparseConvTensor(x.features, bad, [4, 5, 6], 2).dense()
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        x.dense()
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        x.dense(channels_first=False)
 
 
 def test_ctor_errors():

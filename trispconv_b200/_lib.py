@@ -42,6 +42,7 @@ CONV_USE_TC = 0x200
 CONV_TC_SIMPLE = 0x400
 HALO_TILE_ROWS = 256  # output rows per tile of tsc_tile_halo
 CONV_NO_RESIDENT_W = 0x800
+CONV_TEST_WAIT_TIMEOUT = 0x1000
 
 W_KCC = 0   # (K, C_in, C_out)
 W_KRSC = 1  # (C_out, kD, kH, kW, C_in)
@@ -195,14 +196,21 @@ def status_word(device: torch.device) -> torch.Tensor:
 _counters: dict = {}
 
 
-def tile_counter(device: torch.device) -> torch.Tensor:
-    """Per-device uint32 through which the persistent conv kernel hands out
-    tiles (zeroed by every conv call on its stream)."""
+def tile_counter(device: torch.device, stream: Optional[int] = None) -> torch.Tensor:
+    """uint32 through which the persistent conv kernel hands out tiles, one
+    per (device, stream): every conv call zeroes its counter on its own
+    stream and its CTAs then take tiles from it, so two calls running at the
+    same time on different streams must not share one (they would reset and
+    consume each other's tile indices).  Calls on one stream are ordered and
+    share it.  `stream` defaults to the device's current stream."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    t = _counters.get(idx)
+    if stream is None:
+        stream = stream_ptr(torch.device("cuda", idx))
+    key = (idx, int(stream))
+    t = _counters.get(key)
     if t is None:
         t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
-        _counters[idx] = t
+        _counters[key] = t
     return t
 
 

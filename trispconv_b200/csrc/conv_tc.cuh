@@ -31,6 +31,7 @@ constexpr int NT = NPROD + 32;      // + MMA warp
 constexpr int KMAX = 64;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per kernel
 constexpr long long kWaitCycles = 4000000000ll;        // bounded barrier waits (~2 s)
+constexpr long long kTestWaitCycles = 200000ll;        // TSC_CONV_TEST_WAIT_TIMEOUT (~0.1 ms)
 
 template <int TN, int KC>
 struct Cfg {
@@ -96,19 +97,20 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 
 constexpr uint32_t kSuspendNs = 50000;  // upper bound of one suspension
 
-// Bounded wait: false on timeout (about kWaitCycles after the wait began) or
-// when another role aborted.  The `deadline` argument is unused and kept for
-// the call sites' symmetry.
+// Bounded wait: false on timeout (about `limit` SM cycles after the wait
+// began, kWaitCycles by default) or when another role aborted.  The
+// `deadline` argument is unused and kept for the call sites' symmetry.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long deadline,
-                                          volatile int* abort_flag, int64_t* status) {
+                                          volatile int* abort_flag, int64_t* status,
+                                          long long limit = kWaitCycles) {
   (void)deadline;
   if (mbar_try_wait(bar, parity)) return true;
   // SM cycle counter (cheap to read, unlike %globaltimer): ~2 s at 2 GHz.
   const long long start = clock64();
   for (;;) {
-    if (mbar_try_wait_sleep(bar, parity, kSuspendNs)) return true;
+    if (mbar_try_wait_sleep(bar, parity, limit < kWaitCycles ? 1000u : kSuspendNs)) return true;
     if (*abort_flag) return false;
-    if (clock64() - start > kWaitCycles) {
+    if (clock64() - start > limit) {
       raise_status(status, TSC_STATUS_WAIT_TIMEOUT);
       *abort_flag = 1;
       return false;

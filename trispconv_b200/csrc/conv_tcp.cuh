@@ -199,7 +199,15 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
   tc::tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
-  if (warp < 4) {
+  if (flags & TSC_CONV_TEST_WAIT_TIMEOUT) {
+    // Testing the bounded waits: with TMEM held and nothing issued, one
+    // thread waits with a short limit on the accumulator-full barrier of
+    // buffer 0, which no role arrives at (no MMA was issued).  The wait runs
+    // out, sets TSC_STATUS_WAIT_TIMEOUT and the abort flag, and every thread
+    // goes to the teardown below, which frees TMEM.  No copy or MMA is in
+    // flight at any point.
+    if (tid == EPI0) tc::mbar_wait(bar_afull, 0u, deadline, s_abort, status, tc::kTestWaitCycles);
+  } else if (warp < 4) {
     // =============================== producers ===============================
     int64_t gstep = 0;  // ring position (same sequence in every producer warp)
     for (int it = 0;; ++it) {

@@ -1207,11 +1207,19 @@ static __device__ __align__(256) unsigned long long g_subm_scratch[size_t{1} << 
 std::mutex g_scratch_mu;
 void* g_scratch_addr[kNoAllocMaxDevices] = {};
 
-// Device address of g_subm_scratch on the current device, looked up once per
-// device (the first call on each device does it).
-int scratch_address(void** out) {
+// Device address of g_subm_scratch on the device that owns `stream`, looked
+// up once per device (the first call on each device does it).  That device
+// must be the current one: the kernels are launched on the current device.
+int scratch_address(cudaStream_t stream, void** out) {
   int dev = 0;
   TSC_CUDA(cudaGetDevice(&dev));
+  int sdev = dev;
+  TSC_CUDA(cudaStreamGetDevice(stream, &sdev));
+  if (sdev != dev) {
+    set_error("the stream belongs to device %d but device %d is current; make the stream's device current",
+              sdev, dev);
+    return TSC_ERR_UNSUPPORTED;
+  }
   if (dev < 0 || dev >= kNoAllocMaxDevices) {
     set_error("device ordinal %d exceeds the %d devices the allocation-free path supports", dev,
               kNoAllocMaxDevices);
@@ -1254,23 +1262,26 @@ int tsc_subm_kmap_noalloc(const int32_t* indices, int64_t n, const tsc_geometry*
     return TSC_ERR_GRID_TOO_LARGE;
   }
   void* scratch = nullptr;
-  rc = scratch_address(&scratch);
+  rc = scratch_address(stream, &scratch);
   if (rc != TSC_OK) return rc;
   const int K = geo->ksize[0] * geo->ksize[1] * geo->ksize[2];
-  TSC_CUDA(cudaMemsetAsync(meta, 0, sizeof(int64_t) * (TSC_META_COUNTS + K), stream));
-  if (n == 0) return TSC_OK;
+  const int64_t meta_words = 2 * static_cast<int64_t>(TSC_META_COUNTS + K);
+  if (n == 0) return fill_words(meta, 0u, meta_words, nullptr, 0u, 0, stream);
   TSC_CHECK_ARG(indices != nullptr && aligned(indices, 16), "indices must be 16-byte aligned");
   TSC_CHECK_ARG(gather_map != nullptr && aligned(gather_map, 4), "gather_map must not be NULL");
   // same table capacity as tsc_subm_kmap; the part in use is reset on every
-  // call because the array keeps the previous call's entries
+  // call because the array keeps the previous call's entries.  From here on
+  // the launches are those of tsc_subm_kmap: meta and table cleared by one
+  // fill kernel, then the build and the query as dependent launches.
   const int log2cap = subm_log2cap(n);
   auto* table = static_cast<unsigned long long*>(scratch);
-  TSC_CUDA(cudaMemsetAsync(table, 0xFF, static_cast<size_t>(8) << log2cap, stream));
+  rc = fill_words(meta, 0u, meta_words, table, 0xFFFFFFFFu, static_cast<int64_t>(2) << log2cap, stream);
+  if (rc != TSC_OK) return rc;
   const GeoDev g = to_dev(*geo);
   const int4* idx = reinterpret_cast<const int4*>(indices);
   const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
-  k_hash_build<<<grid, kThreads, 0, stream>>>(idx, n, g.B, g.D, g.H, g.W, table, log2cap, status);
-  TSC_LAUNCH_CHECK("k_hash_build");
+  TSC_LAUNCH_PDL("k_hash_build", k_hash_build, dim3(grid), dim3(kThreads), 0, stream, idx, n, g.B, g.D, g.H, g.W,
+                 table, log2cap, status);
   return launch_subm_query(idx, n, g, table, log2cap, gather_map, meta, stream);
 }
 

@@ -131,6 +131,8 @@ def conv_launch(features: torch.Tensor, weight: torch.Tensor, weight_layout: int
     b = None if bias is None else _as_dtype(bias.reshape(-1), dtype)
     lib = L.load()
     flags = (L.CONV_RELU if relu else 0) | _FORCE_FLAGS
+    stream = L.stream_ptr(dev)
+    counter = L.tile_counter(dev, stream)
     halo = None
     if (_HALO and gather is not None and order is None and n_in > 0 and dtype != torch.float32
             and weight_layout == L.W_KRSC and km.n_out == n_out):
@@ -144,15 +146,14 @@ def conv_launch(features: torch.Tensor, weight: torch.Tensor, weight_layout: int
         rc = lib.tsc_conv_forward_halo(feats.data_ptr(), L.DTYPE_CODE[dtype], n_in, c_in, w.data_ptr(),
                                        weight_layout, L.ptr(b), gather.data_ptr(), None, k_vol, n_out, c_out,
                                        L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(), flags,
-                                       L.status_word(dev).data_ptr(), L.tile_counter(dev).data_ptr(),
-                                       hrows.data_ptr(), hcount.data_ptr(), hmap.data_ptr(), hcap,
-                                       L.stream_ptr(dev))
+                                       L.status_word(dev).data_ptr(), counter.data_ptr(),
+                                       hrows.data_ptr(), hcount.data_ptr(), hmap.data_ptr(), hcap, stream)
         L.check(rc, "tsc_conv_forward_halo")
     else:
         rc = lib.tsc_conv_forward(feats.data_ptr() if n_in else None, L.DTYPE_CODE[dtype], n_in, c_in,
                                   w.data_ptr(), weight_layout, L.ptr(b), L.ptr(gather), L.ptr(order), k_vol, n_out,
                                   c_out, L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(), flags,
-                                  L.status_word(dev).data_ptr(), L.tile_counter(dev).data_ptr(), L.stream_ptr(dev))
+                                  L.status_word(dev).data_ptr(), counter.data_ptr(), stream)
         L.check(rc, "tsc_conv_forward")
     if L.EAGER_CHECKS:
         L.check_device_status(dev)

@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import os
 import weakref
+from collections import OrderedDict
 from typing import List, Optional, Sequence, Tuple
 
 import torch
@@ -241,8 +242,15 @@ def _eager_check(device: torch.device) -> None:
 # Grids of at most DENSE_MAX_CELLS cells (batch * D * H * W) are mapped through
 # a direct-address int32 table (tsc_subm_kmap_dense) that stays allocated per
 # device and stream and holds -1 between calls; larger grids use the hash.
+# At most DENSE_TABLES_PER_DEVICE tables (the most recently used streams) are
+# kept per device, so the resident memory is bounded by
+# DENSE_TABLES_PER_DEVICE * 4 * DENSE_MAX_CELLS bytes whatever the number of
+# streams.  A table is only ever used on the stream it was allocated on, so
+# dropping one returns its memory to that stream's cache after the work
+# queued there.
 DENSE_MAX_CELLS = int(os.environ.get("TRISPCONV_B200_DENSE_MAX_CELLS", str(1 << 28)))
-_dense_tables: dict = {}
+DENSE_TABLES_PER_DEVICE = 2
+_dense_tables: "OrderedDict" = OrderedDict()
 
 
 def _dense_table(dev: torch.device, stream: int, cells: int) -> torch.Tensor:
@@ -251,6 +259,10 @@ def _dense_table(dev: torch.device, stream: int, cells: int) -> torch.Tensor:
     if t is None or t.numel() < cells:
         t = torch.full((cells,), -1, dtype=torch.int32, device=dev)
         _dense_tables[key] = t
+    _dense_tables.move_to_end(key)
+    same = [k for k in _dense_tables if k[0] == dev.index]
+    for k in same[:-DENSE_TABLES_PER_DEVICE]:
+        del _dense_tables[k]
     return t
 
 

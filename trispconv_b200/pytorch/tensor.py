@@ -60,26 +60,14 @@ class SparseConvTensor:
 
     def dense(self, channels_first: bool = True) -> torch.Tensor:
         """Scatter features into a dense (B, C, D, H, W) (or (B, D, H, W, C))
-        tensor.  On CUDA this is one kernel of libtrispconv_b200.so; on the
-        host (CPU-resident tensors) it is plain tensor indexing.  Coordinates
-        outside the grid raise AssertionError like the reference (:87-91)."""
-        B = self.batch_size
+        tensor with one kernel of libtrispconv_b200.so (tsc_to_dense).  Like
+        every entry point of this package it takes CUDA tensors only: CPU
+        tensors raise RuntimeError.  Coordinates outside the grid raise
+        AssertionError like the reference (tensor.py:87-91)."""
         feats = self._features
-        C = feats.shape[1]
+        L.require_cuda(feats, "features")
         D, H, W = (int(v) for v in self.spatial_shape)
-        if feats.device.type == "cuda":
-            return _dense_cuda(feats, self.indices, B, C, (D, H, W), channels_first)
-        dense = torch.zeros((B, D, H, W, C), dtype=feats.dtype, device=feats.device)
-        idx = self.indices.long()
-        b, z, y, x = idx[:, 0], idx[:, 1], idx[:, 2], idx[:, 3]
-        assert (b >= 0).all() and (b < B).all(), "batch index out of range"
-        assert (z >= 0).all() and (z < D).all(), "z coordinate out of range"
-        assert (y >= 0).all() and (y < H).all(), "y coordinate out of range"
-        assert (x >= 0).all() and (x < W).all(), "x coordinate out of range"
-        dense[b, z, y, x] = feats
-        if not channels_first:
-            return dense
-        return dense.permute(0, 4, 1, 2, 3).contiguous()
+        return _dense_cuda(feats, self.indices, self.batch_size, feats.shape[1], (D, H, W), channels_first)
 
 
 def _dense_cuda(feats: torch.Tensor, indices: torch.Tensor, B: int, C: int, shape, channels_first: bool):

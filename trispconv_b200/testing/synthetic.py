@@ -314,6 +314,14 @@ def config4(seed: int = 4, batch: int = 8, per_sample: int = 200_000,
     return Workload("config4_unet_fp16", idx, feats, shape, batch, layers, np.float16)
 
 
+def config5_sample_coords(b: int, seed: int = 5, per_sample: int = 500_000, shape=(64, 512, 512)) -> np.ndarray:
+    """(z, y, x) of sample b of the config-5 layout drawn from its own seeded
+    generator ([seed, b]), so that a rank (or a worker process) can generate
+    only its own samples.  Same distribution as config5(); not the same draws
+    (config5 draws all samples from one sequential generator)."""
+    return lidar_sample(np.random.default_rng([seed, b]), shape, per_sample)[0]
+
+
 def config5(channels: int = 128, seed: int = 5, batch: int = 16, per_sample: int = 500_000,
             shape=(64, 512, 512)) -> Workload:
     rng = np.random.default_rng(seed)
