@@ -330,7 +330,8 @@ class ConvProbe:
         counts = None if (km is None or km.meta is None or not self.keep_counts) else km.meta[8:8 + km.k_vol]
         self.records.append(dict(kind="conv", start=s, end=e, n_in=features.shape[0], c_in=features.shape[1],
                                  n_out=n_out, c_out=c_out, counts=counts, k_vol=1 if km is None else km.k_vol,
-                                 elem=features.element_size()))
+                                 elem=features.element_size(),
+                                 no_overflow=km is not None and km.gather is not None and km.overflow is None))
         return out
 
     def _wrap(self, fn, kind):
@@ -389,7 +390,7 @@ def layer_table(records, peaks, per_step: int) -> list:
         pipe = tc if s == 2 else FP32_SIMT_TFLOPS * 1e12
         t_roof = max(byt / hbm, flops / pipe)
         rows.append(dict(kind="conv", ms=ms, n_in=r["n_in"], n_out=r["n_out"], c_in=r["c_in"], c_out=r["c_out"],
-                         k_vol=r["k_vol"], elem=s, pairs=P, bytes=byt, flops=flops, bound="hbm" if byt / hbm >= flops / pipe else "tensor",
+                         k_vol=r["k_vol"], elem=s, pairs=P, no_overflow=r.get("no_overflow", False), bytes=byt, flops=flops, bound="hbm" if byt / hbm >= flops / pipe else "tensor",
                          frac=t_roof / (ms / 1e3)))
     return rows
 
@@ -403,7 +404,9 @@ def conv_kernel_name(r: dict, flags: int, halo: bool = False) -> str:
     half = r["elem"] == 2
     if half and not flags & _lib.CONV_FORCE_SIMT:
         if flags & _lib.CONV_USE_TC and c_in % 64 == 0 and c_out % 32 == 0 and k <= 27 and c_out % 8 == 0:
-            return "k_conv_tch" if halo and c_in == 64 else "k_conv_tcp"
+            if halo and c_in == 64 and c_out in (64, 128) and k == 27 and r.get("no_overflow"):
+                return "k_conv_tmh"
+            return "k_conv_tcp"
         if k <= 64 and c_out % 8 == 0 and (c_in % 8 == 0 or (c_in % 4 == 0 and c_in <= 16)):
             return "k_conv_mma"
     return "k_conv_simt"

@@ -113,7 +113,9 @@ TSC_API unsigned long long tsc_launch_count(void);
  * gather_map[k][i] = row j whose coordinate equals coord(i) + (k - K//2)*d,
  * or -1.  With duplicate coordinates j is the LAST such row (the reference's
  * `table[encoded] = arange` write order).  meta[TSC_META_COUNTS + k] receives
- * pair_num[k].  Requires batch*D*H*W <= 2^32 - 2. */
+ * pair_num[k].  Keys are 32-bit up to batch*D*H*W = 2^32 - 2 cells and
+ * 64-bit above (the reference's int64 key, indices.py:45-51), up to 2^62
+ * cells; tsc_subm_kmap_workspace covers both. */
 TSC_API size_t tsc_subm_kmap_workspace(int64_t n);
 TSC_API int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo,
                   void* workspace, size_t workspace_bytes,
@@ -135,7 +137,9 @@ TSC_API int tsc_subm_kmap_dense(const int32_t* indices, int64_t n, const tsc_geo
  * Replaces generate_strided_indice_pairs (indices.py:143-259).  The output
  * set is found with an occupancy bitmap over the output grid (1 bit per
  * cell) and a prefix popcount, which yields the reference's
- * `torch.unique(sorted=True)` order (:219-220) without a sort.
+ * `torch.unique(sorted=True)` order (:219-220) without a sort.  Bitmap
+ * positions are 32-bit up to 2^32 - 2 output cells and 64-bit above, up to
+ * 2^62 output cells (the bitmap takes batch*D*H*W/8 bytes of workspace).
  *
  * Step 1 (count): marks the bitmap, counts pairs per offset and the
  * participating input rows, and writes meta[N_OUT], meta[N_PART] and
@@ -251,39 +255,48 @@ TSC_API int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, 
                      const int32_t* overflow, int64_t overflow_cap, const int64_t* meta,
                      void* out, int32_t flags, int64_t* status, uint32_t* tile_counter, void* stream);
 
-/* ---- per-tile input halos for the convolution ------------------------------
+/* ---- per-plane input halos for the convolution ----------------------------
  * No counterpart in the reference (its CPU path has no tiles): a faster
- * variant of tsc_conv_forward for 16-bit layers with exactly 64 input
- * channels.  The persistent tcgen05 kernel computes tiles of
- * TSC_HALO_TILE_ROWS consecutive output rows; a tile's halo is the list of
- * distinct input rows its pairs read.  tsc_tile_halo lists them once per map
- * so that the convolution loads each distinct input row of a tile once into
- * shared memory instead of once per pair.  Results are identical with and
- * without a halo.
- *   tsc_conv_halo_capacity: halo rows per tile the halo kernel holds for this
- *     layer (dtype, c_in, c_out, K, conv flags), or 0 when it does not apply.
- *   tsc_tile_halo: from a k-major gather map [k_vol][n_out] (1 <= K <= 27)
- *     writes, per tile t = o / TSC_HALO_TILE_ROWS, halo_rows[t][capacity]
- *     (16-byte aligned; the first halo_count[t] entries, padded to a multiple
- *     of 4 with copies of the last one) and halo_map [k_vol][n_out] int16:
- *     the position of gather_map[k][o] in its tile's list, -1 for no pair, -2
- *     for a row beyond the capacity (read from the gather map instead).
- *   tsc_conv_forward_halo: tsc_conv_forward plus the three halo buffers built
- *     with `halo_capacity` == tsc_conv_halo_capacity of the layer.  Layers
- *     the halo kernel does not take (or a row_order) run as in
- *     tsc_conv_forward. */
+ * variant of tsc_conv_forward for 16-bit 3x3x3 layers with 64 input and 64
+ * or 128 output channels on maps whose output rows are spatially ordered
+ * (the outputs of a strided map and the submanifold maps built on them).
+ * The persistent tcgen05 kernel computes tiles of TSC_HALO_TILE_ROWS
+ * consecutive output rows.  A plane is one kz of the kernel (offsets
+ * k = p*kH*kW .. +kH*kW-1); the sub-halo of (tile, plane) lists the distinct
+ * input rows the plane's pairs of the tile read, ascending.  The kernel
+ * loads each sub-halo once into shared memory (TMA gather4) and builds the A
+ * operand of every pair from it in tensor memory, instead of fetching an
+ * input row from L2 once per pair.  Results are identical with and without
+ * halos (same pairs, same offset order, same fp32 accumulation).
+ *   tsc_conv_halo_capacity: rows per (tile, plane) sub-halo the halo kernel
+ *     holds for this layer (dtype, c_in, c_out, K, conv flags), or 0 when it
+ *     does not apply.
+ *   tsc_tile_halo: from a k-major gather map [k_vol][n_out] (K <= 32,
+ *     `planes` dividing K) writes, per tile t = o / TSC_HALO_TILE_ROWS and
+ *     plane p, halo_rows[t][p][capacity] (16-byte aligned; the first
+ *     halo_count[t][p] entries, padded to a multiple of 4 with copies of the
+ *     last), plane_kmask[t][p] (bit k set when offset k of the plane has a
+ *     pair in the tile) and halo_map [k_vol][n_out] int16: the position of
+ *     gather_map[k][o] in its (tile, plane) list, -1 for no pair, -2 for a
+ *     row beyond the capacity or a plane whose rows span more than 65536
+ *     rows (read from the gather map instead).
+ *   tsc_conv_forward_halo: tsc_conv_forward plus the four halo buffers built
+ *     with `planes` == 3 and `halo_capacity` == tsc_conv_halo_capacity of the
+ *     layer.  Layers the halo kernel does not take (or a row_order, or an
+ *     overflow list) run as in tsc_conv_forward. */
 #define TSC_HALO_TILE_ROWS 256
 TSC_API int32_t tsc_conv_halo_capacity(int32_t dtype, int32_t c_in, int32_t c_out, int32_t k_vol, int32_t flags);
-TSC_API int tsc_tile_halo(const int32_t* gather_map, int32_t k_vol, int64_t n_in, int64_t n_out, int32_t capacity,
-                  int32_t* halo_rows, int32_t* halo_count, int16_t* halo_map, int64_t* status, void* stream);
+TSC_API int tsc_tile_halo(const int32_t* gather_map, int32_t k_vol, int32_t planes, int64_t n_in, int64_t n_out,
+                  int32_t capacity, int32_t* halo_rows, int32_t* halo_count, uint32_t* plane_kmask,
+                  int16_t* halo_map, int64_t* status, void* stream);
 TSC_API int tsc_conv_forward_halo(const void* features, int32_t dtype, int64_t n_in, int32_t c_in,
                      const void* weight, int32_t weight_layout, const void* bias,
                      const int32_t* gather_map, const int32_t* row_order,
                      int32_t k_vol, int64_t n_out, int32_t c_out,
                      const int32_t* overflow, int64_t overflow_cap, const int64_t* meta,
                      void* out, int32_t flags, int64_t* status, uint32_t* tile_counter,
-                     const int32_t* halo_rows, const int32_t* halo_count, const int16_t* halo_map,
-                     int32_t halo_capacity, void* stream);
+                     const int32_t* halo_rows, const int32_t* halo_count, const uint32_t* plane_kmask,
+                     const int16_t* halo_map, int32_t planes, int32_t halo_capacity, void* stream);
 
 /* ---- dense scatter ---------------------------------------------------------
  * SparseConvTensor.dense() (tensor.py:72-99): writes features into a zeroed
@@ -315,6 +328,8 @@ TSC_API int tsc_row_order(const int32_t* gather_map, int32_t k_vol, int64_t n_ou
  * process exits) instead of a caller workspace; it calls no allocator.
  *   - n must not exceed tsc_subm_kmap_noalloc_max_voxels() (2^20); larger
  *     inputs fail with TSC_ERR_WORKSPACE and a message naming the limit.
+ *     Grids above 2^32 - 2 cells (64-bit keys) fail with
+ *     TSC_ERR_GRID_TOO_LARGE; use tsc_subm_kmap for them.
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
  *   - The current device must be the one that owns `stream` (the array's

@@ -45,9 +45,10 @@ def test_abi_version_and_introspection(lib):
 
 
 def test_workspace_sizes(lib):
-    assert lib.tsc_subm_kmap_workspace(0) == 8 << 8
-    assert lib.tsc_subm_kmap_workspace(1000) == 8 << 11          # 2n rounded up to 2^11
-    assert lib.tsc_subm_kmap_workspace(160000) == 8 << 19
+    # 12 bytes per slot (a 64-bit key + a row, for grids above 2^32 - 2 cells)
+    assert lib.tsc_subm_kmap_workspace(0) == 12 << 8
+    assert lib.tsc_subm_kmap_workspace(1000) == 12 << 11         # 2n rounded up to 2^11
+    assert lib.tsc_subm_kmap_workspace(160000) == 12 << 19
     g = L.make_geometry(4, (41, 1600, 1408), (21, 800, 704), (3, 3, 3), (2, 2, 2), (1, 1, 1))
     ws = lib.tsc_strided_kmap_workspace(ctypes.byref(g))
     bits = 4 * 21 * 800 * 704
@@ -68,10 +69,18 @@ def test_host_side_argument_checks(lib):
     rc = lib.tsc_subm_kmap(None, -1, ctypes.byref(g), None, 0, None, ctypes.addressof(m),
                            ctypes.addressof(s), None)
     assert rc == L.TSC_ERR_INVALID_ARG
-    big = L.make_geometry(1 << 20, (1 << 10, 1 << 10, 1 << 10), (4, 4, 4), (3, 3, 3))
+    # 2^63 cells: beyond the 64-bit key range (2^62)
+    big = L.make_geometry(1 << 30, (1 << 11, 1 << 11, 1 << 11), (4, 4, 4), (3, 3, 3))
     rc = lib.tsc_subm_kmap(None, 1, ctypes.byref(big), None, 0, None, ctypes.addressof(m),
                            ctypes.addressof(s), None)
-    assert rc == L.TSC_ERR_GRID_TOO_LARGE
+    assert rc == L.TSC_ERR_GRID_TOO_LARGE and "2^62" in L.last_error()
+    # 2^50 cells: accepted (64-bit keys); the call then stops at its undersized
+    # workspace, before any CUDA call (the pointers are never dereferenced)
+    wide = L.make_geometry(1 << 20, (1 << 10, 1 << 10, 1 << 10), (1 << 10, 1 << 10, 1 << 10), (3, 3, 3))
+    rc = lib.tsc_subm_kmap(1 << 20, 1, ctypes.byref(wide), 1 << 20, 16, 1 << 20, ctypes.addressof(m),
+                           ctypes.addressof(s), None)
+    assert rc == L.TSC_ERR_WORKSPACE and str(lib.tsc_subm_kmap_workspace(1)) in L.last_error()
+    assert lib.tsc_subm_kmap_workspace(1) == 12 << 8
     rc = lib.tsc_conv_forward(None, 0, 10, 0, None, 0, None, None, None, 27, 10, 8, None, 0, None, None, 0,
                               ctypes.addressof(s), None, None)
     assert rc == L.TSC_ERR_INVALID_ARG

@@ -45,7 +45,9 @@ def test_reference_arm_prints_one_contract_line():
 @pytest.mark.parametrize("c_in,c_out,k,elem,flags,halo,want", [
     (64, 64, 27, 2, _lib.CONV_USE_TC, False, "k_conv_tcp"),
     (64, 128, 3, 2, _lib.CONV_USE_TC, False, "k_conv_tcp"),
-    (64, 64, 27, 2, _lib.CONV_USE_TC, True, "k_conv_tch"),
+    (64, 64, 27, 2, _lib.CONV_USE_TC, True, "k_conv_tmh"),
+    (64, 128, 27, 2, _lib.CONV_USE_TC, True, "k_conv_tmh"),
+    (64, 96, 27, 2, _lib.CONV_USE_TC, True, "k_conv_tcp"),
     (128, 128, 27, 2, _lib.CONV_USE_TC, True, "k_conv_tcp"),
     (32, 32, 27, 2, _lib.CONV_USE_TC, False, "k_conv_mma"),
     (4, 16, 27, 2, _lib.CONV_USE_TC, False, "k_conv_mma"),
@@ -55,7 +57,7 @@ def test_reference_arm_prints_one_contract_line():
     (6, 16, 27, 2, _lib.CONV_USE_TC, False, "k_conv_simt"),
 ])
 def test_conv_kernel_name_follows_the_dispatch_rule(c_in, c_out, k, elem, flags, halo, want):
-    r = dict(c_in=c_in, c_out=c_out, k_vol=k, elem=elem)
+    r = dict(c_in=c_in, c_out=c_out, k_vol=k, elem=elem, no_overflow=True)
     assert bench.conv_kernel_name(r, flags, halo) == want
 
 

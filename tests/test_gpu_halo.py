@@ -1,8 +1,10 @@
-"""Per-tile input halos (tsc_tile_halo) and the halo convolution kernel.
+"""Per-plane input sub-halos (tsc_tile_halo) and the halo convolution kernel
+(tensor-memory A operand, conv_tmh.cuh).
 
-The halo kernel (opt-in) issues the same MMAs with the same masks as the
-TMA-gather persistent kernel, only from rows staged differently, so the two
-must agree bit for bit; it is also checked against the oracle."""
+The halo kernel issues the same MMAs (same pairs, same offset order, same
+K=16 steps, fp32 accumulation in tensor memory) as the TMA-gather persistent
+kernel, only with the A operand staged differently, so the two must agree
+bit for bit; it is also checked against the oracle."""
 import numpy as np
 import pytest
 import torch
@@ -18,6 +20,7 @@ from trispconv_b200.pytorch.indices import (build_tile_halo, generate_strided_in
 pytestmark = pytest.mark.gpu
 
 TILE = L.HALO_TILE_ROWS
+PLANES = L.HALO_PLANES
 
 
 def _cloud(rng, shape, n):
@@ -26,57 +29,92 @@ def _cloud(rng, shape, n):
     return np.stack([np.zeros(n), z, y, x], 1).astype(np.int32)
 
 
-def _slab(rng, n, shape=(6, 400, 400)):
-    """Points on a few z-planes: many neighbours per voxel, as on LiDAR maps."""
-    cells = rng.choice(shape[1] * shape[2], n // 3, replace=False)
-    y, x = np.unravel_index(cells, shape[1:])
-    pts = [np.stack([np.zeros_like(y), np.full_like(y, z), y, x], 1) for z in (2, 3, 4)]
-    return np.concatenate(pts).astype(np.int32), shape
+def _slab(rng, n, shape=(6, 400, 400), sort=True, batch=1):
+    """Points on three z-planes (many neighbours per voxel, as on LiDAR
+    maps), in (b, z, y, x) key order when `sort` (the order strided maps
+    emit), else shuffled."""
+    per = []
+    for b in range(batch):
+        cells = rng.choice(shape[1] * shape[2], n // (3 * batch), replace=False)
+        y, x = np.unravel_index(cells, shape[1:])
+        per += [np.stack([np.full_like(y, b), np.full_like(y, z), y, x], 1) for z in (2, 3, 4)]
+    pts = np.concatenate(per).astype(np.int32)
+    if sort:
+        key = ((pts[:, 0].astype(np.int64) * shape[0] + pts[:, 1]) * shape[1] + pts[:, 2]) * shape[2] + pts[:, 3]
+        pts = pts[np.argsort(key)]
+    else:
+        pts = pts[rng.permutation(len(pts))]
+    return np.ascontiguousarray(pts), shape
 
 
-def _check_halo(gather, n_in, cap, rows, count, hmap):
-    """Every (k, o) entry resolves to its input row through the halo."""
+def _check_halo(gather, cap, rows, count, kmask, hmap):
+    """Every (k, o) entry resolves to its input row through its (tile, plane)
+    sub-halo, which lists the plane's distinct rows in ascending order."""
     K, n_out = gather.shape
+    kpg = K // PLANES
     tiles = (n_out + TILE - 1) // TILE
-    rows = rows.reshape(tiles, cap)
+    rows = rows.reshape(tiles, PLANES, cap)
+    count = count.reshape(tiles, PLANES)
+    kmask = kmask.reshape(tiles, PLANES).view(np.uint32)
     assert hmap.shape == (K, n_out)
     for t in range(tiles):
         o0, o1 = t * TILE, min(n_out, (t + 1) * TILE)
-        g = gather[:, o0:o1]
-        h = hmap[:, o0:o1].astype(np.int64)
-        uniq = np.unique(g[g >= 0])
-        c = int(count[t])
-        assert c == min(len(uniq), cap), (t, c, len(uniq))
-        listed = rows[t, :c]
-        assert len(np.unique(listed)) == c and np.isin(listed, uniq).all()
-        # padding to a multiple of 4 repeats the last listed row
-        for i in range(c, (c + 3) // 4 * 4):
-            assert rows[t, i] == listed[-1]
-        assert np.array_equal(h == -1, g < 0)
-        inside = h >= 0
-        assert (h[inside] < c).all()
-        assert np.array_equal(listed[h[inside]], g[inside])
-        outside = h == -2
-        assert (g[outside] >= 0).all()
-        if outside.any():
-            assert c == cap and not np.isin(g[outside], listed).any()
-        else:
-            assert np.isin(uniq, listed).all()
+        for p in range(PLANES):
+            ks = slice(p * kpg, (p + 1) * kpg)
+            g = gather[ks, o0:o1]
+            h = hmap[ks, o0:o1].astype(np.int64)
+            want_mask = sum(1 << (p * kpg + j) for j in range(kpg) if (g[j] >= 0).any())
+            assert int(kmask[t, p]) == want_mask, (t, p)
+            uniq = np.unique(g[g >= 0])
+            c = int(count[t, p])
+            assert np.array_equal(h == -1, g < 0)
+            if c == 0 and len(uniq):
+                # rows too far apart for one ranking window: all from global memory
+                assert (h[g >= 0] == -2).all() and uniq[-1] - uniq[0] >= 65536
+                continue
+            assert c == min(len(uniq), cap), (t, p, c, len(uniq))
+            listed = rows[t, p, :c]
+            assert np.array_equal(listed, uniq[:c]), "sub-halo must list the distinct rows in ascending order"
+            for i in range(c, (c + 3) // 4 * 4):
+                assert rows[t, p, i] == listed[-1]
+            inside = h >= 0
+            assert np.array_equal(listed[h[inside]], g[inside])
+            outside = h == -2
+            if outside.any():  # ranks past the capacity: the largest rows
+                assert c == cap and (g[outside] > listed[-1]).all()
 
 
-@pytest.mark.parametrize("cap", [1120, 64, 8])
-def test_tile_halo_lists_every_input_once(cuda, cap):
+@pytest.mark.parametrize("cap", [640, 64, 8])
+def test_tile_halo_lists_every_input_once_per_plane(cuda, cap):
     rng = np.random.default_rng(cap)
-    idx, shape = _slab(rng, 30_000)
-    it = torch.from_numpy(idx).to(cuda)
-    for kind in ("subm", "spconv"):
-        data = (generate_subm_indice_pairs(it, shape, 1, 3) if kind == "subm" else
-                generate_strided_indice_pairs(it, shape, 1, 3, 2, 1))
-        km = data._kmap
-        _, rows, count, hmap = build_tile_halo(km, cap, len(idx))
-        torch.cuda.synchronize()
-        L.check_device_status(cuda)
-        _check_halo(np_(km.gather), len(idx), cap, np_(rows), np_(count), np_(hmap))
+    for sort in (True, False):
+        idx, shape = _slab(rng, 30_000, sort=sort)
+        it = torch.from_numpy(idx).to(cuda)
+        for kind in ("subm", "spconv"):
+            data = (generate_subm_indice_pairs(it, shape, 1, 3) if kind == "subm" else
+                    generate_strided_indice_pairs(it, shape, 1, 3, 2, 1))
+            km = data._kmap
+            _, rows, count, kmask, hmap = build_tile_halo(km, cap, len(idx))
+            torch.cuda.synchronize()
+            L.check_device_status(cuda)
+            _check_halo(np_(km.gather), cap, np_(rows), np_(count), np_(kmask), np_(hmap))
+
+
+def test_tile_halo_rows_beyond_one_window(cuda):
+    """A shuffled cloud over more than 65536 rows: planes whose rows span
+    more than one ranking window list nothing and send every pair to global
+    memory."""
+    rng = np.random.default_rng(4)
+    shape = (60, 60, 60)
+    n = 150_000
+    idx = torch.from_numpy(_cloud(rng, shape, n)).to(cuda)
+    km = generate_subm_indice_pairs(idx, shape, 1, 3)._kmap
+    _, rows, count, kmask, hmap = build_tile_halo(km, 640, n)
+    torch.cuda.synchronize()
+    c = np_(count)
+    assert (c == 0).any()
+    _check_halo(np_(km.gather)[:, :20 * TILE], 640, np_(rows)[:20 * PLANES * 640], c[:20 * PLANES],
+                np_(kmask)[:20 * PLANES], np_(hmap)[:, :20 * TILE])
 
 
 def _conv_pair(m, x_fn):
@@ -98,28 +136,29 @@ def _conv_pair(m, x_fn):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
-@pytest.mark.parametrize("cout", [32, 64, 96, 128, 256])
-def test_halo_kernel_bit_identical_to_gather_kernel(cuda, dtype, cout):
-    rng = np.random.default_rng(cout)
-    idx, shape = _slab(rng, 60_000)
+@pytest.mark.parametrize("cout", [64, 128])
+@pytest.mark.parametrize("n,sort,batch", [(60_000, True, 1), (60_000, False, 1), (20_001, True, 3), (700, True, 1)])
+def test_halo_kernel_bit_identical_to_gather_kernel(cuda, dtype, cout, n, sort, batch):
+    rng = np.random.default_rng(cout + n)
+    idx, shape = _slab(rng, n, sort=sort, batch=batch)
     it = torch.from_numpy(idx).to(cuda)
     f = torch.from_numpy(rng.standard_normal((len(idx), 64)).astype(np.float32)).to(cuda, dtype)
-    for kind in ("subm", "spconv"):
-        m = (spconv.SubMConv3d(64, cout, 3) if kind == "subm" else
-             spconv.SparseConv3d(64, cout, 3, stride=2, padding=1)).to(cuda, dtype)
-        with torch.no_grad():
-            m.weight.mul_(0.5)
-            m.bias.normal_(0, 0.1)
-        x = spconv.SparseConvTensor(f, it, shape, 1)
-        a, b = _conv_pair(m, lambda: spconv.SparseConvTensor(f, it, shape, 1, indice_dict=x.indice_dict))
-        assert torch.isfinite(a.features).all()
-        assert torch.equal(a.indices, b.indices)
-        assert torch.equal(a.features, b.features), f"{kind} 64->{cout}"
+    m = spconv.SubMConv3d(64, cout, 3, indice_key="s").to(cuda, dtype)
+    with torch.no_grad():
+        m.weight.mul_(0.5)
+        m.bias.normal_(0, 0.1)
+    x = spconv.SparseConvTensor(f, it, shape, batch)
+    a, b = _conv_pair(m, lambda: spconv.SparseConvTensor(f, it, shape, batch, indice_dict=x.indice_dict))
+    assert x.indice_dict["s"]._kmap.halo is not None, "the halo kernel was not used"
+    assert torch.isfinite(a.features).all()
+    assert torch.equal(a.indices, b.indices)
+    assert torch.equal(a.features, b.features), f"64->{cout} n={n} sorted={sort}"
 
 
 def test_halo_kernel_is_used_and_cached(cuda):
-    """A 64-channel fp16 layer builds the map's halo once; a second layer on
-    the same map reuses it."""
+    """A 64-channel fp16 layer builds the map's halos once; a second layer on
+    the same map reuses them; strided maps (overflow lists) keep the
+    TMA-gather kernel."""
     rng = np.random.default_rng(3)
     idx, shape = _slab(rng, 20_000)
     it = torch.from_numpy(idx).to(cuda)
@@ -132,35 +171,15 @@ def test_halo_kernel_is_used_and_cached(cuda):
     try:
         y = net(x)
         km = x.indice_dict["s"]._kmap
-        first_map = km.halo
+        first = km.halo
         net(spconv.SparseConvTensor(f, it, shape, 1, indice_dict=x.indice_dict))
     finally:
         Fn.set_tile_halo(prev)
     assert km.halo is not None and km.halo[0] == L.load().tsc_conv_halo_capacity(
         L.DTYPE_CODE[torch.float16], 64, 64, 27, L.CONV_USE_TC)
-    assert km.halo is first_map
+    assert km.halo is first
     torch.cuda.synchronize()
     assert torch.isfinite(y.features).all()
-
-
-def test_halo_overflow_rows_read_from_global(cuda):
-    """A scattered cloud: most tiles have more distinct inputs than the halo
-    holds, so many rows take the global-memory path."""
-    rng = np.random.default_rng(11)
-    shape = (40, 40, 40)
-    n = 30_000
-    idx = torch.from_numpy(_cloud(rng, shape, n)).to(cuda)
-    data = generate_subm_indice_pairs(idx, shape, 1, 3)
-    km = data._kmap
-    cap = L.load().tsc_conv_halo_capacity(L.DTYPE_CODE[torch.float16], 64, 64, 27, L.CONV_USE_TC)
-    _, rows, count, hmap = build_tile_halo(km, cap, n)
-    torch.cuda.synchronize()
-    assert (np_(hmap) == -2).sum() > 0 and int(np_(count).max()) == cap
-    f = torch.from_numpy(rng.standard_normal((n, 64)).astype(np.float32)).to(cuda).half()
-    m = spconv.SubMConv3d(64, 64, 3, indice_key="s").to(cuda).half()
-    x = spconv.SparseConvTensor(f, idx, shape, 1)
-    a, b = _conv_pair(m, lambda: spconv.SparseConvTensor(f, idx, shape, 1, indice_dict=x.indice_dict))
-    assert torch.equal(a.features, b.features)
 
 
 def test_halo_kernel_vs_oracle(cuda):

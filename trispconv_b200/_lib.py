@@ -41,6 +41,7 @@ CONV_FORCE_SIMT = 0x100
 CONV_USE_TC = 0x200
 CONV_TC_SIMPLE = 0x400
 HALO_TILE_ROWS = 256  # output rows per tile of tsc_tile_halo
+HALO_PLANES = 3  # kz planes of a 3x3x3 kernel (the halo kernel's plane split)
 CONV_NO_RESIDENT_W = 0x800
 CONV_TEST_WAIT_TIMEOUT = 0x1000
 
@@ -101,10 +102,10 @@ _SIGNATURES = {
     "tsc_conv_forward": (ctypes.c_int, [_P, c_int32, c_int64, c_int32, _P, c_int32, _P, _P, _P, c_int32,
                                         c_int64, c_int32, _P, c_int64, _P, _P, c_int32, _P, _P, _P]),
     "tsc_conv_halo_capacity": (c_int32, [c_int32, c_int32, c_int32, c_int32, c_int32]),
-    "tsc_tile_halo": (ctypes.c_int, [_P, c_int32, c_int64, c_int64, c_int32, _P, _P, _P, _P, _P]),
+    "tsc_tile_halo": (ctypes.c_int, [_P, c_int32, c_int32, c_int64, c_int64, c_int32, _P, _P, _P, _P, _P, _P]),
     "tsc_conv_forward_halo": (ctypes.c_int, [_P, c_int32, c_int64, c_int32, _P, c_int32, _P, _P, _P, c_int32,
                                              c_int64, c_int32, _P, c_int64, _P, _P, c_int32, _P, _P, _P, _P, _P,
-                                             c_int32, _P]),
+                                             _P, c_int32, c_int32, _P]),
     "tsc_to_dense": (ctypes.c_int, [_P, c_int32, _P, c_int64, c_int32, c_int32, _P, c_int32, _P, _P, _P]),
     "tsc_row_order_workspace": (c_size_t, [c_int64]),
     "tsc_row_order": (ctypes.c_int, [_P, c_int32, c_int64, _P, c_size_t, _P, _P, _P]),

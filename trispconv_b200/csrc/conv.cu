@@ -259,9 +259,9 @@ int conv_forward(const ConvArgs& a, int32_t dtype, int32_t weight_layout) {
     if ((flags & TSC_CONV_TC_SIMPLE) != 0 && tc_eligible(dtype, w_krsc, c_in, c_out, k_vol))
       return f16 ? launch_tc_f16(a) : launch_tc_bf16(a);
     if (n_in > 0 && (flags & TSC_CONV_TC_SIMPLE) == 0 && a.halo_map != nullptr && a.gather_map != nullptr &&
-        a.row_order == nullptr && tch_eligible(dtype, w_krsc, c_in, c_out, k_vol) &&
-        a.halo_capacity == tch_capacity(c_out))
-      return f16 ? launch_tch_f16(a) : launch_tch_bf16(a);
+        a.row_order == nullptr && a.overflow == nullptr && a.halo_planes == 3 &&
+        tmh_eligible(dtype, w_krsc, c_in, c_out, k_vol) && a.halo_capacity == tmh_capacity(c_out))
+      return f16 ? launch_tmh_f16(a) : launch_tmh_bf16(a);
     if (n_in > 0 && tcp_eligible(dtype, w_krsc, c_in, c_out, k_vol) && (flags & TSC_CONV_TC_SIMPLE) == 0)
       return f16 ? launch_tcp_f16(a) : launch_tcp_bf16(a);
   }
@@ -305,23 +305,27 @@ int tsc_conv_forward_halo(const void* features, int32_t dtype, int64_t n_in, int
                           const int32_t* row_order, int32_t k_vol, int64_t n_out, int32_t c_out,
                           const int32_t* overflow, int64_t overflow_cap, const int64_t* meta, void* out,
                           int32_t flags, int64_t* status, uint32_t* tile_counter, const int32_t* halo_rows,
-                          const int32_t* halo_count, const int16_t* halo_map, int32_t halo_capacity, void* stream) {
-  TSC_CHECK_ARG(halo_map == nullptr || (halo_rows != nullptr && halo_count != nullptr && aligned(halo_rows, 16)),
-                "halo_map needs halo_rows (16-byte aligned) and halo_count");
+                          const int32_t* halo_count, const uint32_t* plane_kmask, const int16_t* halo_map,
+                          int32_t planes, int32_t halo_capacity, void* stream) {
+  TSC_CHECK_ARG(halo_map == nullptr || (halo_rows != nullptr && halo_count != nullptr && plane_kmask != nullptr &&
+                                        aligned(halo_rows, 16)),
+                "halo_map needs halo_rows (16-byte aligned), halo_count and plane_kmask");
   ConvArgs a{features, n_in,     c_in,  weight, bias,   gather_map,   row_order,
              k_vol,    n_out,    c_out, overflow, overflow_cap, meta, out,
              flags,    status,   tile_counter, static_cast<cudaStream_t>(stream)};
   a.halo_rows = halo_rows;
   a.halo_count = halo_count;
+  a.plane_kmask = plane_kmask;
   a.halo_map = halo_map;
+  a.halo_planes = planes;
   a.halo_capacity = halo_capacity;
   return conv_forward(a, dtype, weight_layout);
 }
 
 int32_t tsc_conv_halo_capacity(int32_t dtype, int32_t c_in, int32_t c_out, int32_t k_vol, int32_t flags) {
   if ((flags & TSC_CONV_USE_TC) == 0 || (flags & (TSC_CONV_TC_SIMPLE | TSC_CONV_FORCE_SIMT)) != 0) return 0;
-  if (!tch_eligible(dtype, 1, c_in, c_out, k_vol)) return 0;
-  return tch_capacity(c_out);
+  if (!tmh_eligible(dtype, 1, c_in, c_out, k_vol)) return 0;
+  return tmh_capacity(c_out);
 }
 
 int tsc_to_dense(const void* features, int32_t dtype, const int32_t* indices, int64_t n, int32_t c,

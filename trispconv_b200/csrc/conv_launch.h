@@ -29,10 +29,12 @@ struct ConvArgs {
   int64_t* status;
   uint32_t* tile_counter;  // persistent kernel: dynamic tile hand-out (NULL = round robin)
   cudaStream_t stream;
-  // per-tile input halos (tsc_tile_halo); NULL = none
+  // per-plane input sub-halos (tsc_tile_halo); NULL = none
   const int32_t* halo_rows = nullptr;
   const int32_t* halo_count = nullptr;
+  const uint32_t* plane_kmask = nullptr;
   const int16_t* halo_map = nullptr;
+  int halo_planes = 0;
   int halo_capacity = 0;
 };
 
@@ -68,15 +70,17 @@ inline bool tcp_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
   return tc_eligible(dtype, w_krsc, c_in, c_out, K) && c_in % 64 == 0 && c_out % 32 == 0 && K <= kPersistentKMax;
 }
 
-// halo kernel (persistent tcgen05, tile inputs staged once in shared
-// memory): the persistent kernel's shapes with exactly 64 input channels.
-inline bool tch_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
-  return tcp_eligible(dtype, w_krsc, c_in, c_out, K) && c_in == 64;
+// halo kernel (persistent tcgen05, per-plane sub-halos staged once in shared
+// memory, A operand in tensor memory): 3x3x3 kernels (3 planes of 9
+// offsets), exactly 64 input channels and 64 or 128 output channels, maps
+// without duplicate-coordinate overflow pairs.
+inline bool tmh_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
+  return tcp_eligible(dtype, w_krsc, c_in, c_out, K) && c_in == 64 && (c_out == 64 || c_out == 128) && K == 27;
 }
 
-// Halo rows per tile the halo kernel holds in shared memory for c_out
-// output channels (depends on the tile width it picks).
-int tch_capacity(int c_out);
+// Rows per (tile, plane) sub-halo the halo kernel holds for c_out output
+// channels (0 when it does not take c_out).
+int tmh_capacity(int c_out);
 
 int launch_mma_f16(const ConvArgs& a);
 int launch_mma_bf16(const ConvArgs& a);
@@ -84,7 +88,7 @@ int launch_tc_f16(const ConvArgs& a);
 int launch_tc_bf16(const ConvArgs& a);
 int launch_tcp_f16(const ConvArgs& a);
 int launch_tcp_bf16(const ConvArgs& a);
-int launch_tch_f16(const ConvArgs& a);
-int launch_tch_bf16(const ConvArgs& a);
+int launch_tmh_f16(const ConvArgs& a);
+int launch_tmh_bf16(const ConvArgs& a);
 
 }  // namespace tsc

@@ -9,7 +9,8 @@
 #include "conv_launch.h"
 #include "conv_mma.cuh"
 #include "conv_tc.cuh"
-#include "conv_tch.cuh"
+#include "conv_tmh.cuh"
+#include <cstdlib>
 #include "conv_tcp.cuh"
 #include "tsc_common.cuh"
 
@@ -266,16 +267,17 @@ int launch_tcp(const void* F, int64_t n_in, int c_in, const void* W, const void*
 }
 
 
-// ---- persistent tcgen05 path with per-tile halos (C_in == 64) --------------------
+// ---- persistent tcgen05 path with per-plane halos, A in tensor memory ---------
 
-template <typename T, int TN>
-int launch_tch_tn(const ConvArgs& a) {
-  using C = tch::Cfg<TN>;
-  auto kern = tch::k_conv_tch<T, TN>;
+template <typename T, int TN, int NS>
+int launch_tmh_tn(const ConvArgs& a) {
+  using C = tmh::Cfg<TN, NS>;
+  auto kern = tmh::k_conv_tmh<T, TN, NS>;
   const T* f = static_cast<const T*>(a.features);
   const T* w = static_cast<const T*>(a.weight);
   CUtensorMap mf, mw;
-  int rc = encode_maps<T, TN, tch::KC>(f, a.n_in, a.c_in, w, a.k_vol, a.c_out, &mf, &mw);
+  // gather4 rows of 64 channels (the whole row) and weight boxes {64, 1, TN}
+  int rc = encode_maps<T, TN, tmh::KC>(f, a.n_in, a.c_in, w, a.k_vol, a.c_out, &mf, &mw);
   if (rc != TSC_OK) return rc;
   static unsigned long long configured = 0;
   int dev = 0;
@@ -284,41 +286,32 @@ int launch_tch_tn(const ConvArgs& a) {
     TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL));
     configured |= 1ull << (dev & 63);
   }
-  const int64_t tiles = ceil_div(a.n_out, tch::BMT) * ceil_div(a.c_out, TN);
+  const int64_t tiles = ceil_div(a.n_out, tmh::BMT);
   const int64_t grid = tiles < sm_count() ? tiles : sm_count();
-  if (a.tile_counter != nullptr) {
-    rc = fill_words(a.tile_counter, 0u, 1, nullptr, 0u, 0, a.stream);
-    if (rc != TSC_OK) return rc;
-  }
-  TSC_LAUNCH_PDL("k_conv_tch", kern, dim3(static_cast<unsigned>(grid)), dim3(tch::NT), C::TOTAL, a.stream, mf, mw, f,
-                 a.n_in, w, static_cast<const T*>(a.bias), a.gather_map, a.k_vol, a.n_out, a.c_out, a.overflow,
-                 a.overflow_cap, a.meta, static_cast<T*>(a.out), a.flags, a.status, a.tile_counter, a.halo_rows,
-                 a.halo_count, a.halo_map);
+  TSC_LAUNCH_PDL("k_conv_tmh", kern, dim3(static_cast<unsigned>(grid)), dim3(tmh::NT), C::TOTAL, a.stream, mf, mw, f,
+                 a.n_in, static_cast<const T*>(a.bias), a.gather_map, a.n_out, a.halo_rows, a.halo_count,
+                 a.plane_kmask, a.halo_map, a.halo_capacity, static_cast<T*>(a.out), a.flags, a.status);
   return TSC_OK;
 }
 
-// Tile width of the halo kernel: the largest UMMA N that divides c_out.
-inline int tch_tile_width(int c_out) {
-  return c_out % 256 == 0 ? 256 : (c_out % 128 == 0 ? 128 : (c_out % 64 == 0 ? 64 : 32));
+inline int tmh_capacity_of(int c_out) {
+  return c_out == 64 ? tmh::Cfg<64, 4>::HALO : (c_out == 128 ? tmh::Cfg<128, 4>::HALO : 0);
 }
 
-inline int tch_capacity_of(int c_out) {
-  switch (tch_tile_width(c_out)) {
-    case 256: return tch::Cfg<256>::HALO;
-    case 128: return tch::Cfg<128>::HALO;
-    case 64: return tch::Cfg<64>::HALO;
-    default: return tch::Cfg<32>::HALO;
-  }
+// Stage count of the 64-channel halo kernel: TRISPCONV_B200_TMH_STAGES (4 or
+// 6; 6 leaves one accumulator buffer), read once.
+inline int tmh_stages() {
+  static int ns = [] {
+    const char* e = std::getenv("TRISPCONV_B200_TMH_STAGES");
+    return (e != nullptr && std::atoi(e) == 6) ? 6 : 4;
+  }();
+  return ns;
 }
 
 template <typename T>
-int launch_tch(const ConvArgs& a) {
-  switch (tch_tile_width(a.c_out)) {
-    case 256: return launch_tch_tn<T, 256>(a);
-    case 128: return launch_tch_tn<T, 128>(a);
-    case 64: return launch_tch_tn<T, 64>(a);
-    default: return launch_tch_tn<T, 32>(a);
-  }
+int launch_tmh(const ConvArgs& a) {
+  if (a.c_out == 64) return tmh_stages() == 6 ? launch_tmh_tn<T, 64, 6>(a) : launch_tmh_tn<T, 64, 4>(a);
+  return launch_tmh_tn<T, 128, 4>(a);
 }
 
 template <typename T>

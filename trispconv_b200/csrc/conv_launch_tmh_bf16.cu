@@ -3,6 +3,6 @@
 
 namespace tsc {
 
-int launch_tch_bf16(const ConvArgs& a) { return detail::launch_tch<__nv_bfloat16>(a); }
+int launch_tmh_bf16(const ConvArgs& a) { return detail::launch_tmh<__nv_bfloat16>(a); }
 
 }  // namespace tsc

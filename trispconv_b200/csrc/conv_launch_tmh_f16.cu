@@ -4,8 +4,8 @@
 
 namespace tsc {
 
-int launch_tch_f16(const ConvArgs& a) { return detail::launch_tch<__half>(a); }
+int launch_tmh_f16(const ConvArgs& a) { return detail::launch_tmh<__half>(a); }
 
-int tch_capacity(int c_out) { return detail::tch_capacity_of(c_out); }
+int tmh_capacity(int c_out) { return detail::tmh_capacity_of(c_out); }
 
 }  // namespace tsc

@@ -1,24 +1,28 @@
-// Per-tile input halos for the halo convolution kernel (conv_tch.cuh).
+// Per-plane input sub-halos for the tensor-memory halo convolution
+// (conv_tmh.cuh).
 //
-// A tile is 256 consecutive output rows of a k-major gather map.  Its halo
-// is the list of distinct input rows that any (offset, row) pair of the tile
-// reads.  For every pair the halo map holds the input row's position in that
-// list, so the convolution kernel can fetch each distinct input row of a tile
-// once into shared memory and build all of the tile's A operands from there.
+// A tile is TSC_HALO_TILE_ROWS (256) consecutive output rows of a k-major
+// gather map; a plane is one kz of the kernel (offsets
+// k = plane*kH*kW .. +kH*kW-1).  The sub-halo of (tile, plane) is the list of
+// distinct input rows that the plane's pairs of the tile read, in ascending
+// row order.  For every pair the halo map holds the input row's position in
+// that list, so the convolution fetches each distinct input row of a
+// (tile, plane) once and builds the A operands of the plane's offsets from it.
 //
-// One CTA per tile:
-//   1. insert the tile's valid gather entries into an open-addressing table
-//      in shared memory (8192 slots > 256 rows x 27 offsets, so an insert
-//      always finds a slot);
-//   2. number the occupied slots (block-wide prefix sum of per-thread
-//      counts); the first `capacity` numbers form the halo list, padded to a
-//      multiple of 4 rows with copies of its last row (TMA gathers 4 rows);
-//   3. rewrite every entry of the tile as its halo position, kOutsideHalo
-//      when the position is >= capacity (the kernel reads those rows from
-//      global memory), or kNoPair.
-// Halo positions depend on the order of the atomic inserts; the
-// convolution's results do not (each output row still accumulates its pairs
-// in offset order from the same input values).
+// One CTA per (tile, plane), one thread per tile row:
+//   1. the smallest and largest input row the (tile, plane) reads;
+//   2. when they lie within kWindow rows of each other (spatially ordered
+//      maps: the outputs of strided maps and the submanifold maps built on
+//      them span a few hundred rows per plane), one bit per row of that
+//      window in shared memory, set by every pair; a prefix popcount over
+//      the window ranks the distinct rows in ascending order.  The first
+//      `capacity` ranks form the list, padded to a multiple of 4 with copies
+//      of its last row (TMA gathers 4 rows);
+//   3. every pair's entry becomes its rank, kOutsideHalo when the rank is
+//      >= capacity or the rows span more than the window (the convolution
+//      reads those rows from global memory), or kNoPair.
+// Also written: plane_kmask[tile][plane], bit k set when offset k of the
+// plane has a pair in the tile.
 #include <cstdint>
 
 #include "tsc_common.cuh"
@@ -27,120 +31,157 @@ namespace tsc {
 namespace {
 
 constexpr int kTileRows = TSC_HALO_TILE_ROWS;
-constexpr int kLog2Slots = 13;
-constexpr int kSlots = 1 << kLog2Slots;
-constexpr int kMaxK = 27;  // kTileRows * kMaxK < kSlots
-static_assert(kTileRows * kMaxK < kSlots, "halo table must never fill");
 constexpr int kThreads = kTileRows;
-constexpr int kSlotsPerThread = kSlots / kThreads;  // 32
-static_assert(kSlotsPerThread == 32, "slot ownership assumes 32 slots per thread");
+constexpr int kWindowWords = 2048;            // bits for 65536 consecutive input rows
+constexpr int kWindow = kWindowWords * 32;
+constexpr int kWordsPerThread = kWindowWords / kThreads;  // 8
+static_assert(kWordsPerThread * kThreads == kWindowWords, "window words per thread");
+constexpr int kMaxK = 32;                     // plane_kmask is one 32-bit word
 constexpr int kNoPair = -1;
 constexpr int kOutsideHalo = -2;
 
-__device__ __forceinline__ uint32_t slot_of(int32_t key) {
-  return (static_cast<uint32_t>(key) * 2654435761u) >> (32 - kLog2Slots);
-}
-
-__device__ __forceinline__ void table_insert(int32_t* keys, int32_t key) {
-  uint32_t h = slot_of(key);
-  for (int p = 0; p < kSlots; ++p) {
-    const int32_t prev = atomicCAS(&keys[h], 0, key);
-    if (prev == 0 || prev == key) return;
-    h = (h + 1) & (kSlots - 1);
-  }
-}
-
-__device__ __forceinline__ int table_find(const int32_t* keys, const int32_t* ids, int32_t key) {
-  uint32_t h = slot_of(key);
-  for (int p = 0; p < kSlots; ++p) {
-    const int32_t k = keys[h];
-    if (k == key) return ids[h];
-    if (k == 0) return -1;
-    h = (h + 1) & (kSlots - 1);
-  }
-  return -1;
-}
-
-__global__ void __launch_bounds__(kThreads) k_tile_halo(const int32_t* __restrict__ gmap, int K, int64_t n_in,
-                                                        int64_t n_out, int cap, int32_t* __restrict__ halo_rows,
-                                                        int32_t* __restrict__ halo_count,
-                                                        int16_t* __restrict__ hmap, int64_t* __restrict__ status) {
-  extern __shared__ int32_t sh[];
-  int32_t* keys = sh;           // input row + 1; 0 = empty
-  int32_t* ids = sh + kSlots;   // halo position of the slot's row
-  __shared__ int32_t s_warp[kThreads / 32];
+__global__ void __launch_bounds__(kThreads) k_tile_plane_halo(const int32_t* __restrict__ gmap, int K, int kpg,
+                                                              int planes, int64_t n_in, int64_t n_out, int cap,
+                                                              int32_t* __restrict__ halo_rows,
+                                                              int32_t* __restrict__ halo_count,
+                                                              uint32_t* __restrict__ plane_kmask,
+                                                              int16_t* __restrict__ hmap,
+                                                              int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ uint32_t bits[kWindowWords];
+  __shared__ uint32_t word_pre[kWindowWords];
+  __shared__ uint32_t warp_sums[32];
+  __shared__ int s_lo, s_hi;
+  __shared__ unsigned s_kmask;
   const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
   const int64_t tile = blockIdx.x;
+  const int plane = blockIdx.y;
+  const int k0 = plane * kpg;
   const int64_t o = tile * kTileRows + tid;
   const bool row_ok = o < n_out;
+  const int64_t hp = tile * planes + plane;  // (tile, plane) index
 
-  for (int i = tid; i < kSlots; i += kThreads) keys[i] = 0;
+  if (tid == 0) {
+    s_lo = 0x7fffffff;
+    s_hi = -1;
+    s_kmask = 0u;
+  }
   __syncthreads();
-  for (int k = 0; k < K; ++k) {
-    int v = row_ok ? __ldg(&gmap[static_cast<int64_t>(k) * n_out + o]) : -1;
+  int lo = 0x7fffffff, hi = -1;
+  unsigned km = 0u;
+  for (int j = 0; j < kpg; ++j) {
+    int v = row_ok ? __ldg(&gmap[static_cast<int64_t>(k0 + j) * n_out + o]) : -1;
     if (v >= n_in) {
       raise_status(status, TSC_STATUS_KEY_RANGE);
       v = -1;
     }
-    if (v >= 0) table_insert(keys, v + 1);
+    if (v >= 0) {
+      lo = min(lo, v);
+      hi = max(hi, v);
+      km |= 1u << (k0 + j);
+    }
   }
+  // warp-level reduction first, then one shared atomic per warp
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    lo = min(lo, __shfl_xor_sync(kFullMask, lo, d));
+    hi = max(hi, __shfl_xor_sync(kFullMask, hi, d));
+    km |= __shfl_xor_sync(kFullMask, km, d);
+  }
+  if ((tid & 31) == 0) {
+    atomicMin(&s_lo, lo);
+    atomicMax(&s_hi, hi);
+    atomicOr(&s_kmask, km);
+  }
+  for (int i = tid; i < kWindowWords; i += kThreads) bits[i] = 0u;
   __syncthreads();
+  const int base = s_lo;
+  const bool any = s_hi >= 0;
+  const bool windowed = any && static_cast<int64_t>(s_hi) - base < kWindow;
+  if (tid == 0) plane_kmask[hp] = s_kmask;
+  int32_t* list = halo_rows + hp * static_cast<int64_t>(cap);
 
-  // thread tid owns slots 32*tid .. 32*tid+31, visited in a lane-rotated
-  // order so that a warp's reads fall into distinct banks
-  int cnt = 0;
-#pragma unroll
-  for (int i = 0; i < kSlotsPerThread; ++i) cnt += keys[tid * kSlotsPerThread + ((i + lane) & 31)] != 0;
-  int incl = cnt;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    const int y = __shfl_up_sync(kFullMask, incl, d);
-    if (lane >= d) incl += y;
+  if (!windowed) {
+    // no pair, or rows too far apart to rank in one window: empty list, and
+    // every pair reads its row from global memory
+    if (tid == 0) halo_count[hp] = 0;
+    if (!row_ok) return;
+    for (int j = 0; j < kpg; ++j) {
+      const int v = __ldg(&gmap[static_cast<int64_t>(k0 + j) * n_out + o]);
+      hmap[static_cast<int64_t>(k0 + j) * n_out + o] =
+          static_cast<int16_t>(v >= 0 && v < n_in ? kOutsideHalo : kNoPair);
+    }
+    return;
   }
-  if (lane == 31) s_warp[warp] = incl;
-  __syncthreads();
-  int before = 0, total = 0;
-#pragma unroll
-  for (int w = 0; w < kThreads / 32; ++w) {
-    before += w < warp ? s_warp[w] : 0;
-    total += s_warp[w];
-  }
-  int id = before + incl - cnt;
-  int32_t* list = halo_rows + tile * static_cast<int64_t>(cap);
-#pragma unroll
-  for (int i = 0; i < kSlotsPerThread; ++i) {
-    const int s = tid * kSlotsPerThread + ((i + lane) & 31);
-    const int32_t key = keys[s];
-    if (key != 0) {
-      ids[s] = id;
-      if (id < cap) list[id] = key - 1;
-      ++id;
+
+  for (int j = 0; j < kpg; ++j) {
+    const int v = row_ok ? __ldg(&gmap[static_cast<int64_t>(k0 + j) * n_out + o]) : -1;
+    if (v >= 0 && v < n_in) {
+      const int b = v - base;
+      atomicOr(&bits[b >> 5], 1u << (b & 31));
     }
   }
   __syncthreads();
-  const int hc = total < cap ? total : cap;
+  // ranks: exclusive prefix of the popcounts, thread tid owning words
+  // tid*8 .. tid*8+7
+  uint32_t cnt = 0;
+#pragma unroll
+  for (int i = 0; i < kWordsPerThread; ++i) cnt += __popc(bits[tid * kWordsPerThread + i]);
+  uint32_t total = 0;
+  uint32_t run = block_exclusive_scan(cnt, warp_sums, &total);
+#pragma unroll
+  for (int i = 0; i < kWordsPerThread; ++i) {
+    const int w = tid * kWordsPerThread + i;
+    word_pre[w] = run;
+    uint32_t m = bits[w];
+    while (m) {
+      const int bit = __ffs(m) - 1;
+      m &= m - 1;
+      if (run < static_cast<uint32_t>(cap)) list[run] = base + w * 32 + bit;
+      ++run;
+    }
+  }
+  const int hc = total < static_cast<uint32_t>(cap) ? static_cast<int>(total) : cap;
+  __syncthreads();
+  // pad the list to a multiple of 4 rows with its last row (the thread that
+  // ranked that row knows it: recompute from the window instead of reading
+  // another thread's global write)
+  if (tid == 0) halo_count[hp] = hc;
   if (tid < 3 && hc > 0) {
     const int i = hc + tid;
-    if (i < ((hc + 3) & ~3)) list[i] = list[hc - 1];
+    if (i < ((hc + 3) & ~3)) {
+      // find the row of rank hc-1
+      const uint32_t want = static_cast<uint32_t>(hc - 1);
+      int lo_w = 0, hi_w = kWindowWords - 1;
+      while (lo_w < hi_w) {  // last word whose prefix is <= want
+        const int mid = (lo_w + hi_w + 1) >> 1;
+        if (word_pre[mid] <= want) lo_w = mid; else hi_w = mid - 1;
+      }
+      uint32_t m = bits[lo_w];
+      uint32_t r = word_pre[lo_w];
+      int bit = 0;
+      while (m) {
+        bit = __ffs(m) - 1;
+        m &= m - 1;
+        if (r == want) break;
+        ++r;
+      }
+      list[i] = base + lo_w * 32 + bit;
+    }
   }
-  if (tid == 0) halo_count[tile] = hc;
-
-  for (int k = 0; k < K; ++k) {
-    if (!row_ok) break;
-    const int v = __ldg(&gmap[static_cast<int64_t>(k) * n_out + o]);
+  if (!row_ok) return;
+  for (int j = 0; j < kpg; ++j) {
+    const int v = __ldg(&gmap[static_cast<int64_t>(k0 + j) * n_out + o]);
     int hv = kNoPair;
     if (v >= 0 && v < n_in) {
-      const int p = table_find(keys, ids, v + 1);
-      hv = p < 0 ? kNoPair : (p < cap ? p : kOutsideHalo);
-      if (p < 0) raise_status(status, TSC_STATUS_INTERNAL);
+      const int b = v - base;
+      const uint32_t rank = word_pre[b >> 5] + __popc(bits[b >> 5] & ((1u << (b & 31)) - 1u));
+      hv = rank < static_cast<uint32_t>(cap) ? static_cast<int>(rank) : kOutsideHalo;
     }
-    hmap[static_cast<int64_t>(k) * n_out + o] = static_cast<int16_t>(hv);
+    hmap[static_cast<int64_t>(k0 + j) * n_out + o] = static_cast<int16_t>(hv);
   }
 }
-
-constexpr int kSmemBytes = 2 * kSlots * static_cast<int>(sizeof(int32_t));
 
 }  // namespace
 }  // namespace tsc
@@ -149,29 +190,26 @@ using namespace tsc;
 
 extern "C" {
 
-int tsc_tile_halo(const int32_t* gather_map, int32_t k_vol, int64_t n_in, int64_t n_out, int32_t capacity,
-                  int32_t* halo_rows, int32_t* halo_count, int16_t* halo_map, int64_t* status, void* stream_) {
+int tsc_tile_halo(const int32_t* gather_map, int32_t k_vol, int32_t planes, int64_t n_in, int64_t n_out,
+                  int32_t capacity, int32_t* halo_rows, int32_t* halo_count, uint32_t* plane_kmask,
+                  int16_t* halo_map, int64_t* status, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   TSC_CHECK_ARG(k_vol >= 1 && k_vol <= kMaxK, "halo maps take 1..%d kernel offsets, got %d", kMaxK, k_vol);
+  TSC_CHECK_ARG(planes >= 1 && k_vol % planes == 0, "%d planes do not divide %d kernel offsets", planes, k_vol);
   TSC_CHECK_ARG(capacity >= 4 && capacity % 4 == 0 && capacity <= 32767,
                 "halo capacity must be a multiple of 4 in [4, 32767], got %d", capacity);
   TSC_CHECK_ARG(n_in >= 0 && n_in <= 0x7fffffffLL && n_out >= 0 && n_out <= 0x7fffffffLL, "row counts out of range");
   TSC_CHECK_ARG(status != nullptr, "status is NULL");
   if (n_out == 0) return TSC_OK;
-  TSC_CHECK_ARG(gather_map != nullptr && halo_rows != nullptr && halo_count != nullptr && halo_map != nullptr,
+  TSC_CHECK_ARG(gather_map != nullptr && halo_rows != nullptr && halo_count != nullptr && plane_kmask != nullptr &&
+                    halo_map != nullptr,
                 "NULL buffer");
   TSC_CHECK_ARG(aligned(halo_rows, 16), "halo_rows must be 16-byte aligned");
-  static unsigned long long configured = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
-    TSC_CUDA(cudaFuncSetAttribute(k_tile_halo, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    configured |= 1ull << (dev & 63);
-  }
   const int64_t tiles = ceil_div(n_out, kTileRows);
-  k_tile_halo<<<static_cast<unsigned>(tiles), kThreads, kSmemBytes, stream>>>(
-      gather_map, k_vol, n_in, n_out, capacity, halo_rows, halo_count, halo_map, status);
-  TSC_LAUNCH_CHECK("k_tile_halo");
+  TSC_CHECK_ARG(tiles <= 0x7fffffffLL, "too many tiles");
+  TSC_LAUNCH_PDL("k_tile_plane_halo", k_tile_plane_halo, dim3(static_cast<unsigned>(tiles), planes), dim3(kThreads), 0,
+                 stream, gather_map, k_vol, k_vol / planes, planes, n_in, n_out, capacity, halo_rows, halo_count,
+                 plane_kmask, halo_map, status);
   return TSC_OK;
 }
 

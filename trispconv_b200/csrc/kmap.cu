@@ -23,7 +23,8 @@ constexpr int kThreads = 256;
 constexpr int kItems = 8;                          // words / flags per thread in scans
 constexpr int kTile = kThreads * kItems;           // 2048 per block
 constexpr int kScanBlockThreads = 1024;
-constexpr uint64_t kMaxCells = 0xFFFFFFFEull;      // keys must stay below the empty sentinel
+constexpr uint64_t kMaxCells = 0xFFFFFFFEull;      // 32-bit keys must stay below the empty sentinel
+constexpr uint64_t kMaxCells64 = 1ull << 62;         // 64-bit keys (grids above kMaxCells)
 
 struct GeoDev {
   int B, D, H, W;
@@ -70,6 +71,21 @@ __device__ __forceinline__ bool in_grid(const int4& c, int B, int D, int H, int 
 __device__ __forceinline__ uint32_t cell_key(unsigned b, unsigned z, unsigned y, unsigned x,
                                              unsigned D, unsigned H, unsigned W) {
   return ((b * D + z) * H + y) * W + x;
+}
+
+// The same key in KeyT: uint32_t for grids of at most kMaxCells cells,
+// uint64_t above (the reference's int64 key, grids up to kMaxCells64).
+template <typename KeyT>
+__device__ __forceinline__ KeyT cell_key_t(unsigned b, unsigned z, unsigned y, unsigned x, unsigned D, unsigned H,
+                                           unsigned W) {
+  return ((static_cast<KeyT>(b) * D + z) * H + y) * W + x;
+}
+
+// Slot of a 64-bit cell key: Fibonacci hashing of key >> 3, keeping the low 3
+// bits (the same neighbourhood-preserving layout as hash_slot).
+__device__ __forceinline__ uint32_t hash_slot64(unsigned long long key, int log2cap) {
+  const uint32_t hi = static_cast<uint32_t>(((key >> 3) * 0x9E3779B97F4A7C15ull) >> (64 - (log2cap - 3)));
+  return (hi << 3) | static_cast<uint32_t>(key & 7u);
 }
 
 // ---------------------------------------------------------------------------
@@ -123,17 +139,75 @@ __device__ __forceinline__ int hash_lookup(const unsigned long long* __restrict_
   return -1;
 }
 
-// Lookups of a packed cell key: in the open-addressing hash, or in a
-// direct-address table (one int32 row per cell, -1 = empty).
+// Grids above kMaxCells: keys and rows in two arrays of 2^log2cap slots
+// (keys kEmptySlot and rows -1 when empty).  atomicCAS claims a key slot;
+// atomicMax on its row keeps the largest row of a duplicated coordinate,
+// the reference's last-write-wins `table[key] = arange(N)` (indices.py:63).
+__global__ void __launch_bounds__(kThreads)
+k_hash_build64(const int4* __restrict__ idx, int64_t n, int B, int D, int H, int W,
+               unsigned long long* __restrict__ keys, int32_t* __restrict__ rows, int log2cap,
+               int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int4 c = idx[i];
+  if (!in_grid(c, B, D, H, W)) {
+    raise_status(status, TSC_STATUS_KEY_RANGE);
+    return;
+  }
+  const unsigned long long key = cell_key_t<unsigned long long>(c.x, c.y, c.z, c.w, D, H, W);
+  const uint32_t mask = (1u << log2cap) - 1u;
+  uint32_t slot = hash_slot64(key, log2cap);
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    unsigned long long cur = keys[slot];
+    if (cur == kEmptySlot) cur = atomicCAS(&keys[slot], kEmptySlot, key);
+    if (cur == kEmptySlot || cur == key) {
+      atomicMax(&rows[slot], static_cast<int32_t>(i));
+      return;
+    }
+    slot = (slot + 1u) & mask;
+  }
+  raise_status(status, TSC_STATUS_HASH_FULL);
+}
+
+// Lookups of a cell (b, z, y, x) of the (D, H, W) grid: in the 32-bit-key
+// open-addressing hash, the 64-bit-key hash, or a direct-address table (one
+// int32 row per cell, -1 = empty).
 struct HashLookup {
   const unsigned long long* table;
   int log2cap;
-  __device__ __forceinline__ int operator()(uint32_t key) const { return hash_lookup(table, log2cap, key); }
+  unsigned D, H, W;
+  __device__ __forceinline__ int operator()(unsigned b, unsigned z, unsigned y, unsigned x) const {
+    return hash_lookup(table, log2cap, cell_key(b, z, y, x, D, H, W));
+  }
+};
+
+struct HashLookup64 {
+  const unsigned long long* keys;
+  const int32_t* rows;
+  int log2cap;
+  unsigned D, H, W;
+  __device__ __forceinline__ int operator()(unsigned b, unsigned z, unsigned y, unsigned x) const {
+    const unsigned long long key = cell_key_t<unsigned long long>(b, z, y, x, D, H, W);
+    const uint32_t mask = (1u << log2cap) - 1u;
+    uint32_t slot = hash_slot64(key, log2cap);
+    for (uint32_t probe = 0; probe <= mask; ++probe) {
+      const unsigned long long e = __ldg(&keys[slot]);
+      if (e == kEmptySlot) return -1;
+      if (e == key) return __ldg(&rows[slot]);
+      slot = (slot + 1u) & mask;
+    }
+    return -1;
+  }
 };
 
 struct DenseLookup {
   const int32_t* table;
-  __device__ __forceinline__ int operator()(uint32_t key) const { return __ldg(&table[key]); }
+  unsigned D, H, W;
+  __device__ __forceinline__ int operator()(unsigned b, unsigned z, unsigned y, unsigned x) const {
+    return __ldg(&table[cell_key(b, z, y, x, D, H, W)]);
+  }
 };
 
 // One thread per (offset k = blockIdx.y, row i).  Writes gather_map[k][i] and
@@ -159,7 +233,7 @@ k_subm_query(const int4* __restrict__ idx, int64_t n, GeoDev g, Lookup look,
         static_cast<unsigned>(nz) < static_cast<unsigned>(g.D) &&
         static_cast<unsigned>(ny) < static_cast<unsigned>(g.H) &&
         static_cast<unsigned>(nx) < static_cast<unsigned>(g.W)) {
-      found = look(cell_key(c.x, nz, ny, nx, g.D, g.H, g.W));
+      found = look(c.x, nz, ny, nx);
     }
     gmap[static_cast<int64_t>(k) * n + i] = found;
   }
@@ -202,7 +276,7 @@ k_subm_query_rows(const int4* __restrict__ idx, int64_t n, GeoDev g, Lookup look
         const int nx = c.w + (kx - g.kW / 2) * g.dx;
         int found = -1;
         if (zy_ok && static_cast<unsigned>(nx) < static_cast<unsigned>(g.W))
-          found = look(cell_key(c.x, nz, ny, nx, g.D, g.H, g.W));
+          found = look(c.x, nz, ny, nx);
         if (row) gmap[static_cast<int64_t>(k) * n + i] = found;
         const unsigned hits = __ballot_sync(kFullMask, found >= 0);
         if (lane == 0 && hits) atomicAdd(&s_cnt[k], static_cast<unsigned>(__popc(hits)));
@@ -233,7 +307,10 @@ int launch_subm_query(const int4* idx, int64_t n, const GeoDev& g, Lookup look, 
 
 int launch_subm_query(const int4* idx, int64_t n, const GeoDev& g, const unsigned long long* table, int log2cap,
                       int32_t* gmap, int64_t* meta, cudaStream_t stream) {
-  return launch_subm_query(idx, n, g, HashLookup{table, log2cap}, gmap, meta, stream);
+  return launch_subm_query(idx, n, g,
+                           HashLookup{table, log2cap, static_cast<unsigned>(g.D), static_cast<unsigned>(g.H),
+                                      static_cast<unsigned>(g.W)},
+                           gmap, meta, stream);
 }
 
 // Direct-address table: the largest row of each cell (the reference's
@@ -287,6 +364,7 @@ __device__ __forceinline__ bool exact_div(int c, int s, int lim, int& o) {
 // Per input row, walks the K offsets in reference order (indices.py:177-187):
 // c = i + p - k*d is a valid output position iff c >= 0, c % s == 0 and
 // c / s < out (for c >= 0 C and Python division agree).
+template <typename KeyT>
 __global__ void __launch_bounds__(kThreads)
 k_strided_mark(const int4* __restrict__ idx, int64_t n, GeoDev g, uint32_t* __restrict__ bitmap,
                unsigned long long* __restrict__ meta, int64_t* __restrict__ status) {
@@ -322,10 +400,10 @@ k_strided_mark(const int4* __restrict__ idx, int64_t n, GeoDev g, uint32_t* __re
         const unsigned b = __ballot_sync(kFullMask, v);
         if (v) {
           // Lanes that hit the same bitmap word combine their bits; one atomic per word.
-          const uint32_t lin = cell_key(c.x, oz, oy, ox, g.oD, g.oH, g.oW);
-          const uint32_t word = lin >> 5;
+          const KeyT lin = cell_key_t<KeyT>(c.x, oz, oy, ox, g.oD, g.oH, g.oW);
+          const KeyT word = lin >> 5;
           const unsigned same = __match_any_sync(b, word);
-          const unsigned bits = __reduce_or_sync(same, 1u << (lin & 31u));
+          const unsigned bits = __reduce_or_sync(same, 1u << static_cast<unsigned>(lin & 31u));
           if (lane == __ffs(same) - 1) atomicOr(&bitmap[word], bits);
           any = true;
         }
@@ -430,6 +508,7 @@ k_bitmap_prefix(const uint4* __restrict__ bitmap, const uint32_t* __restrict__ t
 // One thread per bitmap word: decode its set bits to coordinates at their
 // rank (a grid of one thread per word keeps sparse and dense grids alike
 // fully parallel).
+template <typename KeyT>
 __global__ void __launch_bounds__(kThreads)
 k_bitmap_coords(const uint32_t* __restrict__ bitmap, const uint32_t* __restrict__ word_prefix,
                 int64_t nwords, GeoDev g, int4* __restrict__ out_idx, int64_t n_out) {
@@ -440,18 +519,18 @@ k_bitmap_coords(const uint32_t* __restrict__ bitmap, const uint32_t* __restrict_
   uint32_t wv = __ldg(&bitmap[w]);
   if (wv == 0) return;
   uint32_t r = __ldg(&word_prefix[w]);
-  const unsigned oW = g.oW, oH = g.oH, oD = g.oD;
+  const KeyT oW = g.oW, oH = g.oH, oD = g.oD;
   {
     while (wv) {
       const int bit = __ffs(wv) - 1;
       wv &= wv - 1u;
-      const uint32_t lin = static_cast<uint32_t>(w * 32 + bit);
-      const uint32_t x = lin % oW;
-      uint32_t t = lin / oW;
-      const uint32_t y = t % oH;
+      const KeyT lin = static_cast<KeyT>(w) * 32 + static_cast<KeyT>(bit);
+      const KeyT x = lin % oW;
+      KeyT t = lin / oW;
+      const KeyT y = t % oH;
       t /= oH;
-      const uint32_t z = t % oD;
-      const uint32_t bb = t / oD;
+      const KeyT z = t % oD;
+      const KeyT bb = t / oD;
       if (r < n_out)
         out_idx[r] = make_int4(static_cast<int>(bb), static_cast<int>(z), static_cast<int>(y),
                                static_cast<int>(x));
@@ -477,6 +556,7 @@ __device__ __forceinline__ void push_overflow(int32_t* overflow, int64_t cap,
 // input-stationary scatter map and (first writer wins) to the
 // output-stationary gather map.  A second input row for the same (k, o) can
 // only come from duplicate input coordinates; it goes to the overflow list.
+template <typename KeyT>
 __global__ void __launch_bounds__(kThreads)
 k_strided_pairs(const int4* __restrict__ idx, int64_t n, GeoDev g,
                 const uint32_t* __restrict__ bitmap, const uint32_t* __restrict__ word_prefix,
@@ -501,10 +581,10 @@ k_strided_pairs(const int4* __restrict__ idx, int64_t n, GeoDev g,
         const bool v = vy && exact_div(c.w + g.px - kx * g.dx, g.sx, g.oW, ox);
         int o = -1;
         if (v) {
-          const uint32_t lin = cell_key(c.x, oz, oy, ox, g.oD, g.oH, g.oW);
-          const uint32_t w = lin >> 5;
+          const KeyT lin = cell_key_t<KeyT>(c.x, oz, oy, ox, g.oD, g.oH, g.oW);
+          const KeyT w = lin >> 5;
           o = static_cast<int>(__ldg(&word_prefix[w]) +
-                               __popc(__ldg(&bitmap[w]) & ((1u << (lin & 31u)) - 1u)));
+                               __popc(__ldg(&bitmap[w]) & ((1u << static_cast<unsigned>(lin & 31u)) - 1u)));
           if (o >= n_out) {
             raise_status(status, TSC_STATUS_KEY_RANGE);
             smap[static_cast<int64_t>(k) * n + i] = -1;
@@ -784,9 +864,16 @@ int check_geometry(const tsc_geometry* geo, bool strided) {
   return TSC_OK;
 }
 
+// batch*D*H*W, saturated to UINT64_MAX (every such grid is refused).
 uint64_t cells_of(int32_t batch, const int32_t* s) {
-  return static_cast<uint64_t>(batch) * static_cast<uint64_t>(s[0]) * static_cast<uint64_t>(s[1]) *
-         static_cast<uint64_t>(s[2]);
+  const uint64_t f[4] = {static_cast<uint64_t>(batch < 0 ? 0 : batch), static_cast<uint64_t>(s[0] < 0 ? 0 : s[0]),
+                         static_cast<uint64_t>(s[1] < 0 ? 0 : s[1]), static_cast<uint64_t>(s[2] < 0 ? 0 : s[2])};
+  uint64_t c = 1;
+  for (uint64_t v : f) {
+    if (v != 0 && c > UINT64_MAX / v) return UINT64_MAX;
+    c *= v;
+  }
+  return c;
 }
 
 struct StridedWs {
@@ -821,7 +908,9 @@ using namespace tsc;
 extern "C" {
 
 size_t tsc_subm_kmap_workspace(int64_t n) {
-  return static_cast<size_t>(8) << subm_log2cap(n);
+  // 8-byte key|row slots for grids of at most 2^32-2 cells; above, 8-byte
+  // keys plus 4-byte rows per slot (the larger of the two)
+  return static_cast<size_t>(12) << subm_log2cap(n);
 }
 
 int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo, void* workspace,
@@ -833,20 +922,37 @@ int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo, vo
   TSC_CHECK_ARG(n >= 0 && n <= 0x7fffffffLL, "number of voxels %lld out of range", (long long)n);
   TSC_CHECK_ARG(meta != nullptr && status != nullptr, "meta/status must not be NULL");
   const uint64_t cells = cells_of(geo->batch, geo->in_shape);
-  if (cells > kMaxCells) {
-    set_error("grid batch*D*H*W = %llu exceeds the packed-key limit 2^32-2", (unsigned long long)cells);
+  if (cells > kMaxCells64) {
+    set_error("grid batch*D*H*W = %llu exceeds the 64-bit key limit 2^62", (unsigned long long)cells);
     return TSC_ERR_GRID_TOO_LARGE;
   }
+  const bool wide = cells > kMaxCells;  // 64-bit keys
   const int K = geo->ksize[0] * geo->ksize[1] * geo->ksize[2];
   const int64_t meta_words = 2 * static_cast<int64_t>(TSC_META_COUNTS + K);
   if (n == 0) return fill_words(meta, 0u, meta_words, nullptr, 0u, 0, stream);
   TSC_CHECK_ARG(indices != nullptr && aligned(indices, 16), "indices must be 16-byte aligned");
   TSC_CHECK_ARG(gather_map != nullptr && aligned(gather_map, 4), "gather_map must not be NULL");
   const int log2cap = subm_log2cap(n);
-  const size_t need = static_cast<size_t>(8) << log2cap;
+  const size_t need = static_cast<size_t>(wide ? 12 : 8) << log2cap;
   if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16)) {
     set_error("subm workspace needs %zu bytes (16-byte aligned), got %zu", need, workspace_bytes);
     return TSC_ERR_WORKSPACE;
+  }
+  if (wide) {
+    // keys (all ones = empty) then rows (-1), one fill with meta = 0
+    auto* keys = static_cast<unsigned long long*>(workspace);
+    auto* rows = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + (static_cast<size_t>(8) << log2cap));
+    rc = fill_words(meta, 0u, meta_words, keys, 0xFFFFFFFFu, static_cast<int64_t>(3) << log2cap, stream);
+    if (rc != TSC_OK) return rc;
+    const GeoDev g = to_dev(*geo);
+    const int4* idx = reinterpret_cast<const int4*>(indices);
+    const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
+    TSC_LAUNCH_PDL("k_hash_build64", k_hash_build64, dim3(grid), dim3(kThreads), 0, stream, idx, n, g.B, g.D, g.H,
+                   g.W, keys, rows, log2cap, status);
+    return launch_subm_query(idx, n, g,
+                             HashLookup64{keys, rows, log2cap, static_cast<unsigned>(g.D), static_cast<unsigned>(g.H),
+                                          static_cast<unsigned>(g.W)},
+                             gather_map, meta, stream);
   }
   auto* table = static_cast<unsigned long long*>(workspace);
   // meta = 0 and every table slot empty (all ones), one launch
@@ -885,7 +991,10 @@ int tsc_subm_kmap_dense(const int32_t* indices, int64_t n, const tsc_geometry* g
   const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
   TSC_LAUNCH_PDL("k_dense_build", k_dense_build, dim3(grid), dim3(kThreads), 0, stream, idx, n, g.B, g.D, g.H, g.W,
                  table, status);
-  rc = launch_subm_query(idx, n, g, DenseLookup{table}, gather_map, meta, stream);
+  rc = launch_subm_query(idx, n, g,
+                         DenseLookup{table, static_cast<unsigned>(g.D), static_cast<unsigned>(g.H),
+                                     static_cast<unsigned>(g.W)},
+                         gather_map, meta, stream);
   if (rc != TSC_OK) return rc;
   TSC_LAUNCH_PDL("k_dense_clear", k_dense_clear, dim3(grid), dim3(kThreads), 0, stream, idx, n, g.B, g.D, g.H, g.W,
                  table);
@@ -894,6 +1003,8 @@ int tsc_subm_kmap_dense(const int32_t* indices, int64_t n, const tsc_geometry* g
 
 size_t tsc_strided_kmap_workspace(const tsc_geometry* geo) {
   if (geo == nullptr) return 0;
+  // grids the count step refuses need no workspace
+  if (cells_of(geo->batch, geo->out_shape) > kMaxCells64) return 0;
   return strided_ws(*geo).bytes;
 }
 
@@ -908,10 +1019,12 @@ int strided_count(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
   if (rc != TSC_OK) return rc;
   TSC_CHECK_ARG(n_in >= 0 && n_in <= 0x7fffffffLL, "number of voxels %lld out of range", (long long)n_in);
   TSC_CHECK_ARG(meta != nullptr && status != nullptr, "meta/status must not be NULL");
-  if (cells_of(geo->batch, geo->out_shape) > kMaxCells) {
-    set_error("output grid batch*D*H*W exceeds 2^32-2 cells");
+  const uint64_t out_cells = cells_of(geo->batch, geo->out_shape);
+  if (out_cells > kMaxCells64 || out_cells / 32 + kTile > static_cast<uint64_t>(INT64_MAX / 64)) {
+    set_error("output grid batch*D*H*W = %llu exceeds the 64-bit key limit 2^62", (unsigned long long)out_cells);
     return TSC_ERR_GRID_TOO_LARGE;
   }
+  const bool wide = out_cells > kMaxCells;  // 64-bit bitmap positions
   TSC_CHECK_ARG(n_in == 0 || (indices != nullptr && aligned(indices, 16)),
                 "indices must be 16-byte aligned");
   const StridedWs w = strided_ws(*geo);
@@ -931,8 +1044,14 @@ int strided_count(const int32_t* indices, int64_t n_in, const tsc_geometry* geo,
   const GeoDev g = to_dev(*geo);
   if (n_in > 0) {
     const unsigned grid = static_cast<unsigned>(ceil_div(n_in, kThreads));
-    TSC_LAUNCH_PDL("k_strided_mark", k_strided_mark, dim3(grid), dim3(kThreads), sizeof(unsigned) * (K + 1), stream,
-                   reinterpret_cast<const int4*>(indices), n_in, g, bitmap, umeta, status);
+    if (wide)
+      TSC_LAUNCH_PDL("k_strided_mark", k_strided_mark<unsigned long long>, dim3(grid), dim3(kThreads),
+                     sizeof(unsigned) * (K + 1), stream, reinterpret_cast<const int4*>(indices), n_in, g, bitmap, umeta,
+                     status);
+    else
+      TSC_LAUNCH_PDL("k_strided_mark", k_strided_mark<uint32_t>, dim3(grid), dim3(kThreads),
+                     sizeof(unsigned) * (K + 1), stream, reinterpret_cast<const int4*>(indices), n_in, g, bitmap, umeta,
+                     status);
   }
   TSC_LAUNCH_PDL("k_bitmap_tile_count", k_bitmap_tile_count, dim3(static_cast<unsigned>(w.nblocks)), dim3(kThreads), 0,
                  stream, reinterpret_cast<const uint4*>(bitmap), sums);
@@ -1007,14 +1126,27 @@ int tsc_strided_kmap_emit(const int32_t* indices, int64_t n_in, const tsc_geomet
   TSC_LAUNCH_PDL("k_bitmap_prefix", k_bitmap_prefix, dim3(static_cast<unsigned>(w.nblocks)), dim3(kThreads), 0,
                  stream, reinterpret_cast<const uint4*>(bitmap), static_cast<const uint32_t*>(sums), prefix);
   const int64_t nwords = static_cast<int64_t>((w.nbits + 31) / 32);
-  TSC_LAUNCH_PDL("k_bitmap_coords", k_bitmap_coords, dim3(static_cast<unsigned>(ceil_div(nwords, kThreads))),
-                 dim3(kThreads), 0, stream, static_cast<const uint32_t*>(bitmap), static_cast<const uint32_t*>(prefix),
-                 nwords, g, reinterpret_cast<int4*>(out_indices), n_out);
+  const bool wide = w.nbits > kMaxCells;  // 64-bit bitmap positions (the count step refused larger grids)
+  const unsigned cgrid = static_cast<unsigned>(ceil_div(nwords, kThreads));
+  if (wide)
+    TSC_LAUNCH_PDL("k_bitmap_coords", k_bitmap_coords<unsigned long long>, dim3(cgrid), dim3(kThreads), 0, stream,
+                   static_cast<const uint32_t*>(bitmap), static_cast<const uint32_t*>(prefix), nwords, g,
+                   reinterpret_cast<int4*>(out_indices), n_out);
+  else
+    TSC_LAUNCH_PDL("k_bitmap_coords", k_bitmap_coords<uint32_t>, dim3(cgrid), dim3(kThreads), 0, stream,
+                   static_cast<const uint32_t*>(bitmap), static_cast<const uint32_t*>(prefix), nwords, g,
+                   reinterpret_cast<int4*>(out_indices), n_out);
   const unsigned grid = static_cast<unsigned>(ceil_div(n_in, kThreads));
-  TSC_LAUNCH_PDL("k_strided_pairs", k_strided_pairs, dim3(grid), dim3(kThreads), 0, stream,
-                 reinterpret_cast<const int4*>(indices), n_in, g, static_cast<const uint32_t*>(bitmap),
-                 static_cast<const uint32_t*>(prefix), n_out, gather_map, scatter_map, overflow, overflow_cap,
-                 reinterpret_cast<unsigned long long*>(meta), status);
+  if (wide)
+    TSC_LAUNCH_PDL("k_strided_pairs", k_strided_pairs<unsigned long long>, dim3(grid), dim3(kThreads), 0, stream,
+                   reinterpret_cast<const int4*>(indices), n_in, g, static_cast<const uint32_t*>(bitmap),
+                   static_cast<const uint32_t*>(prefix), n_out, gather_map, scatter_map, overflow, overflow_cap,
+                   reinterpret_cast<unsigned long long*>(meta), status);
+  else
+    TSC_LAUNCH_PDL("k_strided_pairs", k_strided_pairs<uint32_t>, dim3(grid), dim3(kThreads), 0, stream,
+                   reinterpret_cast<const int4*>(indices), n_in, g, static_cast<const uint32_t*>(bitmap),
+                   static_cast<const uint32_t*>(prefix), n_out, gather_map, scatter_map, overflow, overflow_cap,
+                   reinterpret_cast<unsigned long long*>(meta), status);
   return TSC_OK;
 }
 

@@ -134,20 +134,21 @@ def conv_launch(features: torch.Tensor, weight: torch.Tensor, weight_layout: int
     stream = L.stream_ptr(dev)
     counter = L.tile_counter(dev, stream)
     halo = None
-    if (_HALO and gather is not None and order is None and n_in > 0 and dtype != torch.float32
-            and weight_layout == L.W_KRSC and km.n_out == n_out):
+    if (_HALO and gather is not None and order is None and overflow is None and n_in > 0
+            and dtype != torch.float32 and weight_layout == L.W_KRSC and km.n_out == n_out):
         hcap = lib.tsc_conv_halo_capacity(L.DTYPE_CODE[dtype], c_in, c_out, k_vol, flags)
         if hcap > 0:
             halo = km.halo
             if halo is None or halo[0] != hcap:
                 halo = km.halo = build_tile_halo(km, hcap, n_in)
     if halo is not None:
-        hcap, hrows, hcount, hmap = halo
+        hcap, hrows, hcount, hkmask, hmap = halo
         rc = lib.tsc_conv_forward_halo(feats.data_ptr(), L.DTYPE_CODE[dtype], n_in, c_in, w.data_ptr(),
                                        weight_layout, L.ptr(b), gather.data_ptr(), None, k_vol, n_out, c_out,
                                        L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(), flags,
                                        L.status_word(dev).data_ptr(), counter.data_ptr(),
-                                       hrows.data_ptr(), hcount.data_ptr(), hmap.data_ptr(), hcap, stream)
+                                       hrows.data_ptr(), hcount.data_ptr(), hkmask.data_ptr(), hmap.data_ptr(),
+                                       L.HALO_PLANES, hcap, stream)
         L.check(rc, "tsc_conv_forward_halo")
     else:
         rc = lib.tsc_conv_forward(feats.data_ptr() if n_in else None, L.DTYPE_CODE[dtype], n_in, c_in,

@@ -53,8 +53,9 @@ class KernelMap:
              reference-ordered pair lists.
     row_order int32 [n_out] or None: order in which the conv kernel groups
              output rows into tiles (does not change results).
-    halo     None or (capacity, rows, count, halo_map): per-tile input halos
-             (tsc_tile_halo) for the 64-channel tcgen05 conv kernel.
+    halo     None or (capacity, rows, count, plane_kmask, halo_map): per-plane
+             input sub-halos (tsc_tile_halo) for the 64-channel tcgen05 conv
+             kernel.
     """
 
     __slots__ = ("k_vol", "n_in", "n_out", "gather", "scatter", "overflow", "overflow_cap", "meta",
@@ -81,22 +82,24 @@ class KernelMap:
         self.halo = None
 
 
-def build_tile_halo(km: "KernelMap", capacity: int, n_in: int):
-    """Per-tile input halos of `km` (tsc_tile_halo) for a conv kernel holding
-    `capacity` rows per tile over `n_in` feature rows; cached on the map by
-    the caller."""
+def build_tile_halo(km: "KernelMap", capacity: int, n_in: int, planes: int = L.HALO_PLANES):
+    """Per-plane input sub-halos of `km` (tsc_tile_halo) for a conv kernel
+    holding `capacity` rows per (tile, plane) over `n_in` feature rows;
+    cached on the map by the caller.  Returns (capacity, rows, count,
+    plane_kmask, halo_map)."""
     dev = km.device
     n_out = km.n_out
     tiles = (n_out + L.HALO_TILE_ROWS - 1) // L.HALO_TILE_ROWS
-    rows = torch.empty(tiles * capacity, dtype=torch.int32, device=dev)
-    count = torch.empty(tiles, dtype=torch.int32, device=dev)
+    rows = torch.empty(tiles * planes * capacity, dtype=torch.int32, device=dev)
+    count = torch.empty(tiles * planes, dtype=torch.int32, device=dev)
+    kmask = torch.empty(tiles * planes, dtype=torch.int32, device=dev)
     hmap = torch.empty((km.k_vol, n_out), dtype=torch.int16, device=dev)
     lib = L.load()
     with L.on_device(dev):
-        L.check(lib.tsc_tile_halo(km.gather.data_ptr(), km.k_vol, n_in, n_out, capacity, rows.data_ptr(),
-                                  count.data_ptr(), hmap.data_ptr(), L.status_word(dev).data_ptr(),
+        L.check(lib.tsc_tile_halo(km.gather.data_ptr(), km.k_vol, planes, n_in, n_out, capacity, rows.data_ptr(),
+                                  count.data_ptr(), kmask.data_ptr(), hmap.data_ptr(), L.status_word(dev).data_ptr(),
                                   L.stream_ptr(dev)), "tsc_tile_halo")
-    return (capacity, rows, count, hmap)
+    return (capacity, rows, count, kmask, hmap)
 
 
 def build_row_order(km: "KernelMap") -> torch.Tensor:
