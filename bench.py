@@ -318,12 +318,12 @@ class ConvProbe:
         e = self.torch.cuda.Event(enable_timing=True)
         return s, e
 
-    def _conv(self, features, weight, layout, bias, km, n_out, c_out, relu=False):
+    def _conv(self, features, weight, layout, bias, km, n_out, c_out, relu=False, epilogue=None):
         if not self.enabled:
-            return self._orig_conv(features, weight, layout, bias, km, n_out, c_out, relu)
+            return self._orig_conv(features, weight, layout, bias, km, n_out, c_out, relu, epilogue)
         s, e = self._events()
         s.record()
-        out = self._orig_conv(features, weight, layout, bias, km, n_out, c_out, relu)
+        out = self._orig_conv(features, weight, layout, bias, km, n_out, c_out, relu, epilogue)
         e.record()
         # keep only a view of the per-offset pair counts (not the kernel map,
         # whose buffers must return to the caching allocator after the step)

@@ -76,6 +76,12 @@ extern "C" {
                                               limit, which runs out and sets TSC_STATUS_WAIT_TIMEOUT (the
                                               output is left unwritten) */
 
+/* Activations of the convolution epilogue (tsc_conv_extras.act). */
+#define TSC_ACT_NONE       0
+#define TSC_ACT_RELU       1  /* same as TSC_CONV_RELU */
+#define TSC_ACT_LEAKY_RELU 2  /* x >= 0 ? x : act_alpha * x */
+#define TSC_ACT_SILU       3  /* x * sigmoid(x) */
+
 /* Weight layouts accepted by tsc_conv_forward. */
 #define TSC_W_KCC  0  /* (K, C_in, C_out): the reference's internal layout (weight.py:36) */
 #define TSC_W_KRSC 1  /* (C_out, kD, kH, kW, C_in): spconv KRSC, the modules' parameter */
@@ -280,23 +286,48 @@ TSC_API int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, 
  *     gather_map[k][o] in its (tile, plane) list, -1 for no pair, -2 for a
  *     row beyond the capacity or a plane whose rows span more than 65536
  *     rows (read from the gather map instead).
- *   tsc_conv_forward_halo: tsc_conv_forward plus the four halo buffers built
- *     with `planes` == 3 and `halo_capacity` == tsc_conv_halo_capacity of the
- *     layer.  Layers the halo kernel does not take (or a row_order, or an
+ *   The convolution takes the halo buffers through tsc_conv_forward_ex
+ *     (below).  Layers the halo kernel does not take (or a row_order, or an
  *     overflow list) run as in tsc_conv_forward. */
 #define TSC_HALO_TILE_ROWS 256
 TSC_API int32_t tsc_conv_halo_capacity(int32_t dtype, int32_t c_in, int32_t c_out, int32_t k_vol, int32_t flags);
 TSC_API int tsc_tile_halo(const int32_t* gather_map, int32_t k_vol, int32_t planes, int64_t n_in, int64_t n_out,
                   int32_t capacity, int32_t* halo_rows, int32_t* halo_count, uint32_t* plane_kmask,
                   int16_t* halo_map, int64_t* status, void* stream);
-TSC_API int tsc_conv_forward_halo(const void* features, int32_t dtype, int64_t n_in, int32_t c_in,
+
+/* ---- convolution with extras -------------------------------------------------
+ * tsc_conv_forward plus optional extras (extras NULL or zero-filled = none):
+ *   epilogue  scale/shift (float [c_out] each, or NULL): the store becomes
+ *             act(acc * scale[n] + shift[n]) in fp32, rounded once; the
+ *             `bias` argument is then ignored (fold it into shift).  This is
+ *             an eval-mode BatchNorm1d on the features fused into the
+ *             convolution: scale = gamma / sqrt(running_var + eps), shift =
+ *             beta + (bias - running_mean) * scale.  The reference applies it
+ *             as a separate module over x.features (modules.py:320-329).
+ *             act: TSC_ACT_* (TSC_CONV_RELU in flags also selects ReLU),
+ *             act_alpha the LeakyReLU slope.
+ *   halos     the four tsc_tile_halo buffers with halo_planes == 3 and
+ *             halo_capacity == tsc_conv_halo_capacity of the layer (see
+ *             above); NULL halo_map = none. */
+typedef struct tsc_conv_extras {
+  const float* scale;
+  const float* shift;
+  int32_t act;
+  float act_alpha;
+  const int32_t* halo_rows;
+  const int32_t* halo_count;
+  const uint32_t* plane_kmask;
+  const int16_t* halo_map;
+  int32_t halo_planes;
+  int32_t halo_capacity;
+} tsc_conv_extras;
+TSC_API int tsc_conv_forward_ex(const void* features, int32_t dtype, int64_t n_in, int32_t c_in,
                      const void* weight, int32_t weight_layout, const void* bias,
                      const int32_t* gather_map, const int32_t* row_order,
                      int32_t k_vol, int64_t n_out, int32_t c_out,
                      const int32_t* overflow, int64_t overflow_cap, const int64_t* meta,
                      void* out, int32_t flags, int64_t* status, uint32_t* tile_counter,
-                     const int32_t* halo_rows, const int32_t* halo_count, const uint32_t* plane_kmask,
-                     const int16_t* halo_map, int32_t planes, int32_t halo_capacity, void* stream);
+                     const tsc_conv_extras* extras, void* stream);
 
 /* ---- dense scatter ---------------------------------------------------------
  * SparseConvTensor.dense() (tensor.py:72-99): writes features into a zeroed
@@ -317,6 +348,40 @@ TSC_API int tsc_to_dense(const void* features, int32_t dtype, const int32_t* ind
 TSC_API size_t tsc_row_order_workspace(int64_t n_out);
 TSC_API int tsc_row_order(const int32_t* gather_map, int32_t k_vol, int64_t n_out, void* workspace,
                   size_t workspace_bytes, int32_t* row_order, int64_t* status, void* stream);
+
+/* ---- voxelisation: points -> unique voxels ----------------------------------
+ * No counterpart in the reference (its SparseConvTensor takes voxels that
+ * the user built, trispconv/pytorch/tensor.py:12-22): the step before the
+ * sparse convolutions.  points is float32 [n][point_dim] with columns x, y,
+ * z and then point_dim-3 features; batch_ids int32 [n] (NULL: all 0).  A
+ * point lies in voxel v_d = floor((p_d - range_lo_d) / voxel_size_d) for
+ * d = x, y, z (float32 arithmetic, IEEE division) and is kept when
+ * 0 <= v_x < W, 0 <= v_y < H, 0 <= v_z < D and 0 <= b < batch; the others
+ * are dropped (a batch id outside [0, batch) also sets TSC_STATUS_KEY_RANGE).
+ * Voxels come out sorted by their (b, z, y, x) key, the order strided maps
+ * produce, found with an occupancy bitmap over the batch*D*H*W grid (keys
+ * 64-bit above 2^32 - 2 cells).  A voxel's features are the mean of
+ * point_dim columns over its kept points: the max_points points of smallest
+ * index (all when max_points <= 0), summed in ascending index order in fp32.
+ * Step 1 (count) writes meta[TSC_META_N_OUT] = voxels and
+ * meta[TSC_META_N_PART] = points inside the range; step 2 (emit), with the
+ * same workspace, writes coords [n_vox][4] (b, z, y, x), features
+ * [n_vox][point_dim] and num_points [n_vox] (kept points per voxel). */
+typedef struct tsc_voxel_params {
+  int32_t batch;
+  int32_t grid[3];      /* (D, H, W): voxels along z, y, x */
+  float range_lo[3];    /* x, y, z of the grid's lower corner */
+  float voxel_size[3];  /* x, y, z voxel extent */
+  int32_t max_points;   /* points kept per voxel; <= 0 keeps all */
+} tsc_voxel_params;
+TSC_API size_t tsc_voxelize_workspace(const tsc_voxel_params* vp, int64_t n_points);
+TSC_API int tsc_voxelize_count(const float* points, int64_t n, int32_t point_dim, const int32_t* batch_ids,
+                       const tsc_voxel_params* vp, void* workspace, size_t workspace_bytes,
+                       int64_t* meta, int64_t* status, void* stream);
+TSC_API int tsc_voxelize_emit(const float* points, int64_t n, int32_t point_dim, const int32_t* batch_ids,
+                      const tsc_voxel_params* vp, void* workspace, size_t workspace_bytes, int64_t n_vox,
+                      int32_t* coords, float* features, int32_t* num_points, int64_t* meta, int64_t* status,
+                      void* stream);
 
 /* ---- allocation-free submanifold kernel map ------------------------------
  * No counterpart in the reference: an addition for callers that cannot

@@ -63,6 +63,40 @@ class Geometry(ctypes.Structure):
     ]
 
 
+class ConvExtras(ctypes.Structure):
+    """tsc_conv_extras: store epilogue (folded BatchNorm scale/shift,
+    activation) and per-plane input halos of tsc_conv_forward_ex."""
+    _fields_ = [
+        ("scale", c_void_p),
+        ("shift", c_void_p),
+        ("act", c_int32),
+        ("act_alpha", ctypes.c_float),
+        ("halo_rows", c_void_p),
+        ("halo_count", c_void_p),
+        ("plane_kmask", c_void_p),
+        ("halo_map", c_void_p),
+        ("halo_planes", c_int32),
+        ("halo_capacity", c_int32),
+    ]
+
+
+class VoxelParams(ctypes.Structure):
+    """tsc_voxel_params (include/trispconv_b200.h)."""
+    _fields_ = [
+        ("batch", c_int32),
+        ("grid", c_int32 * 3),
+        ("range_lo", ctypes.c_float * 3),
+        ("voxel_size", ctypes.c_float * 3),
+        ("max_points", c_int32),
+    ]
+
+
+ACT_NONE = 0
+ACT_RELU = 1
+ACT_LEAKY_RELU = 2
+ACT_SILU = 3
+
+
 def make_geometry(batch, in_shape, out_shape, ksize, stride=(1, 1, 1), padding=(0, 0, 0),
                   dilation=(1, 1, 1)) -> Geometry:
     g = Geometry()
@@ -103,12 +137,17 @@ _SIGNATURES = {
                                         c_int64, c_int32, _P, c_int64, _P, _P, c_int32, _P, _P, _P]),
     "tsc_conv_halo_capacity": (c_int32, [c_int32, c_int32, c_int32, c_int32, c_int32]),
     "tsc_tile_halo": (ctypes.c_int, [_P, c_int32, c_int32, c_int64, c_int64, c_int32, _P, _P, _P, _P, _P, _P]),
-    "tsc_conv_forward_halo": (ctypes.c_int, [_P, c_int32, c_int64, c_int32, _P, c_int32, _P, _P, _P, c_int32,
-                                             c_int64, c_int32, _P, c_int64, _P, _P, c_int32, _P, _P, _P, _P, _P,
-                                             _P, c_int32, c_int32, _P]),
+    "tsc_conv_forward_ex": (ctypes.c_int, [_P, c_int32, c_int64, c_int32, _P, c_int32, _P, _P, _P, c_int32,
+                                           c_int64, c_int32, _P, c_int64, _P, _P, c_int32, _P, _P,
+                                           POINTER(ConvExtras), _P]),
     "tsc_to_dense": (ctypes.c_int, [_P, c_int32, _P, c_int64, c_int32, c_int32, _P, c_int32, _P, _P, _P]),
     "tsc_row_order_workspace": (c_size_t, [c_int64]),
     "tsc_row_order": (ctypes.c_int, [_P, c_int32, c_int64, _P, c_size_t, _P, _P, _P]),
+    "tsc_voxelize_workspace": (c_size_t, [POINTER(VoxelParams), c_int64]),
+    "tsc_voxelize_count": (ctypes.c_int, [_P, c_int64, c_int32, _P, POINTER(VoxelParams), _P, c_size_t, _P, _P,
+                                          _P]),
+    "tsc_voxelize_emit": (ctypes.c_int, [_P, c_int64, c_int32, _P, POINTER(VoxelParams), _P, c_size_t, c_int64,
+                                         _P, _P, _P, _P, _P, _P]),
     "tsc_subm_kmap_noalloc_max_voxels": (c_int64, []),
     "tsc_subm_kmap_noalloc": (ctypes.c_int, [_P, c_int64, POINTER(Geometry), _P, _P, _P, _P]),
 }

@@ -32,7 +32,7 @@ __global__ void __launch_bounds__(kConvThreads)
 k_conv_simt(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__ Wt, int w_krsc,
             const T* __restrict__ bias, const int32_t* __restrict__ gmap, int K, int64_t n_out,
             int c_out, const int32_t* __restrict__ ovf, int64_t ovf_cap, const int64_t* __restrict__ meta,
-            T* __restrict__ out, int flags, int64_t* __restrict__ status) {
+            T* __restrict__ out, int flags, EpiParams epi, int64_t* __restrict__ status) {
   constexpr int CT = TN / 4;              // threads along output channels
   constexpr int RT = kConvThreads / CT;   // threads along rows
   constexpr int TM = RT * 4;              // rows per CTA
@@ -130,7 +130,6 @@ k_conv_simt(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict
     }
   }
 
-  const bool relu = (flags & TSC_CONV_RELU) != 0;
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const int64_t o = o0 + ty * 4 + r;
@@ -139,10 +138,7 @@ k_conv_simt(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict
     for (int q = 0; q < 4; ++q) {
       const int n = n0 + tx * 4 + q;
       if (n >= c_out) continue;
-      float v = acc[r][q];
-      if (bias != nullptr) v += to_f32(bias[n]);
-      if (relu) v = fmaxf(v, 0.f);
-      out[o * c_out + n] = from_f32<T>(v);
+      out[o * c_out + n] = from_f32<T>(epi_apply(acc[r][q], n, epi, bias));
     }
   }
 }
@@ -150,7 +146,7 @@ k_conv_simt(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict
 template <typename T>
 int launch_simt(const void* F, int64_t n_in, int c_in, const void* W, int w_krsc, const void* bias,
                 const int32_t* gmap, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                const int64_t* meta, void* out, int flags, int64_t* status, cudaStream_t stream) {
+                const int64_t* meta, void* out, int flags, const EpiParams& epi, int64_t* status, cudaStream_t stream) {
   const T* f = static_cast<const T*>(F);
   const T* w = static_cast<const T*>(W);
   const T* bs = static_cast<const T*>(bias);
@@ -159,17 +155,17 @@ int launch_simt(const void* F, int64_t n_in, int c_in, const void* W, int w_krsc
     constexpr int TN = 16, TM = (kConvThreads / (TN / 4)) * 4;
     dim3 grid(static_cast<unsigned>(ceil_div(n_out, TM)), static_cast<unsigned>(ceil_div(c_out, TN)));
     k_conv_simt<T, TN><<<grid, kConvThreads, 0, stream>>>(f, n_in, c_in, w, w_krsc, bs, gmap, K, n_out, c_out,
-                                                          ovf, ovf_cap, meta, o, flags, status);
+                                                          ovf, ovf_cap, meta, o, flags, epi, status);
   } else if (c_out <= 32) {
     constexpr int TN = 32, TM = (kConvThreads / (TN / 4)) * 4;
     dim3 grid(static_cast<unsigned>(ceil_div(n_out, TM)), static_cast<unsigned>(ceil_div(c_out, TN)));
     k_conv_simt<T, TN><<<grid, kConvThreads, 0, stream>>>(f, n_in, c_in, w, w_krsc, bs, gmap, K, n_out, c_out,
-                                                          ovf, ovf_cap, meta, o, flags, status);
+                                                          ovf, ovf_cap, meta, o, flags, epi, status);
   } else {
     constexpr int TN = 64, TM = (kConvThreads / (TN / 4)) * 4;
     dim3 grid(static_cast<unsigned>(ceil_div(n_out, TM)), static_cast<unsigned>(ceil_div(c_out, TN)));
     k_conv_simt<T, TN><<<grid, kConvThreads, 0, stream>>>(f, n_in, c_in, w, w_krsc, bs, gmap, K, n_out, c_out,
-                                                          ovf, ovf_cap, meta, o, flags, status);
+                                                          ovf, ovf_cap, meta, o, flags, epi, status);
   }
   TSC_LAUNCH_CHECK("k_conv_simt");
   return TSC_OK;
@@ -230,7 +226,7 @@ namespace {
 
 // Argument checks and kernel choice shared by tsc_conv_forward and
 // tsc_conv_forward_halo.
-int conv_forward(const ConvArgs& a, int32_t dtype, int32_t weight_layout) {
+int conv_forward(ConvArgs a, int32_t dtype, int32_t weight_layout) {
   const int64_t n_in = a.n_in, n_out = a.n_out;
   const int c_in = a.c_in, c_out = a.c_out, k_vol = a.k_vol, flags = a.flags;
   TSC_CHECK_ARG(c_in > 0 && c_out > 0, "channel counts must be positive (c_in=%d, c_out=%d)", c_in, c_out);
@@ -250,6 +246,15 @@ int conv_forward(const ConvArgs& a, int32_t dtype, int32_t weight_layout) {
   TSC_CHECK_ARG(a.bias == nullptr || aligned(a.bias, 4), "bias must be 4-byte aligned");
   TSC_CHECK_ARG(a.overflow == nullptr || (a.meta != nullptr && a.overflow_cap >= 0),
                 "overflow list needs its meta buffer");
+  TSC_CHECK_ARG(a.epi.act >= TSC_ACT_NONE && a.epi.act <= TSC_ACT_SILU, "unknown activation %d", a.epi.act);
+  TSC_CHECK_ARG((a.epi.scale == nullptr) == (a.epi.shift == nullptr), "epilogue scale and shift go together");
+  TSC_CHECK_ARG(a.epi.scale == nullptr || (aligned(a.epi.scale, 4) && aligned(a.epi.shift, 4)),
+                "epilogue scale/shift must be 4-byte aligned");
+  if ((flags & TSC_CONV_RELU) != 0) {
+    TSC_CHECK_ARG(a.epi.act == TSC_ACT_NONE || a.epi.act == TSC_ACT_RELU,
+                  "TSC_CONV_RELU and activation %d both requested", a.epi.act);
+    a.epi.act = TSC_ACT_RELU;
+  }
   const int w_krsc = weight_layout == TSC_W_KRSC;
   const bool force_simt = (flags & TSC_CONV_FORCE_SIMT) != 0;
   const bool f16 = dtype == TSC_F16;
@@ -272,13 +277,13 @@ int conv_forward(const ConvArgs& a, int32_t dtype, int32_t weight_layout) {
   switch (dtype) {
     case TSC_F32:
       return launch_simt<float>(a.features, n_in, c_in, a.weight, w_krsc, a.bias, a.gather_map, k_vol, n_out, c_out,
-                                a.overflow, a.overflow_cap, a.meta, a.out, flags, a.status, a.stream);
+                                a.overflow, a.overflow_cap, a.meta, a.out, flags, a.epi, a.status, a.stream);
     case TSC_F16:
       return launch_simt<__half>(a.features, n_in, c_in, a.weight, w_krsc, a.bias, a.gather_map, k_vol, n_out, c_out,
-                                 a.overflow, a.overflow_cap, a.meta, a.out, flags, a.status, a.stream);
+                                 a.overflow, a.overflow_cap, a.meta, a.out, flags, a.epi, a.status, a.stream);
     case TSC_BF16:
       return launch_simt<__nv_bfloat16>(a.features, n_in, c_in, a.weight, w_krsc, a.bias, a.gather_map, k_vol, n_out,
-                                        c_out, a.overflow, a.overflow_cap, a.meta, a.out, flags, a.status, a.stream);
+                                        c_out, a.overflow, a.overflow_cap, a.meta, a.out, flags, a.epi, a.status, a.stream);
     default:
       set_error("unsupported dtype code %d for the convolution", dtype);
       return TSC_ERR_UNSUPPORTED;
@@ -300,25 +305,27 @@ int tsc_conv_forward(const void* features, int32_t dtype, int64_t n_in, int32_t 
   return conv_forward(a, dtype, weight_layout);
 }
 
-int tsc_conv_forward_halo(const void* features, int32_t dtype, int64_t n_in, int32_t c_in, const void* weight,
-                          int32_t weight_layout, const void* bias, const int32_t* gather_map,
-                          const int32_t* row_order, int32_t k_vol, int64_t n_out, int32_t c_out,
-                          const int32_t* overflow, int64_t overflow_cap, const int64_t* meta, void* out,
-                          int32_t flags, int64_t* status, uint32_t* tile_counter, const int32_t* halo_rows,
-                          const int32_t* halo_count, const uint32_t* plane_kmask, const int16_t* halo_map,
-                          int32_t planes, int32_t halo_capacity, void* stream) {
-  TSC_CHECK_ARG(halo_map == nullptr || (halo_rows != nullptr && halo_count != nullptr && plane_kmask != nullptr &&
-                                        aligned(halo_rows, 16)),
-                "halo_map needs halo_rows (16-byte aligned), halo_count and plane_kmask");
+int tsc_conv_forward_ex(const void* features, int32_t dtype, int64_t n_in, int32_t c_in, const void* weight,
+                        int32_t weight_layout, const void* bias, const int32_t* gather_map, const int32_t* row_order,
+                        int32_t k_vol, int64_t n_out, int32_t c_out, const int32_t* overflow, int64_t overflow_cap,
+                        const int64_t* meta, void* out, int32_t flags, int64_t* status, uint32_t* tile_counter,
+                        const tsc_conv_extras* extras, void* stream) {
   ConvArgs a{features, n_in,     c_in,  weight, bias,   gather_map,   row_order,
              k_vol,    n_out,    c_out, overflow, overflow_cap, meta, out,
              flags,    status,   tile_counter, static_cast<cudaStream_t>(stream)};
-  a.halo_rows = halo_rows;
-  a.halo_count = halo_count;
-  a.plane_kmask = plane_kmask;
-  a.halo_map = halo_map;
-  a.halo_planes = planes;
-  a.halo_capacity = halo_capacity;
+  if (extras != nullptr) {
+    const tsc_conv_extras& x = *extras;
+    TSC_CHECK_ARG(x.halo_map == nullptr || (x.halo_rows != nullptr && x.halo_count != nullptr &&
+                                            x.plane_kmask != nullptr && aligned(x.halo_rows, 16)),
+                  "halo_map needs halo_rows (16-byte aligned), halo_count and plane_kmask");
+    a.halo_rows = x.halo_rows;
+    a.halo_count = x.halo_count;
+    a.plane_kmask = x.plane_kmask;
+    a.halo_map = x.halo_map;
+    a.halo_planes = x.halo_planes;
+    a.halo_capacity = x.halo_capacity;
+    a.epi = EpiParams{x.scale, x.shift, x.act, x.act_alpha};
+  }
   return conv_forward(a, dtype, weight_layout);
 }
 

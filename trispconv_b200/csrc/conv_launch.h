@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "trispconv_b200.h"
+#include "tsc_common.cuh"
 
 namespace tsc {
 
@@ -36,6 +37,8 @@ struct ConvArgs {
   const int16_t* halo_map = nullptr;
   int halo_planes = 0;
   int halo_capacity = 0;
+  // store epilogue (folded BatchNorm scale/shift, activation); set by conv_forward
+  EpiParams epi = {nullptr, nullptr, TSC_ACT_NONE, 0.f};
 };
 
 // Largest kernel volumes the tensor-core kernels take (gather-map slice in

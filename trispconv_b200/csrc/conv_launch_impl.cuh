@@ -27,7 +27,7 @@ static_assert(mma::KMAX == kMmaKMax && tc::KMAX == kMmaKMax, "kernel K limits");
 template <typename T, int TN, int KC, int CH>
 int launch_mmaw_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                     const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                    const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+                    const int64_t* meta, T* out, int flags, const EpiParams& epi, int64_t* status, cudaStream_t stream) {
   using C = mma::CfgW<TN, KC>;
   auto kern = mma::k_conv_mmaw<T, TN, KC, CH>;
   constexpr int kMaxSmem = C::MAIN + mma::kMaxResidentWeightBytes + (mma::KMAX * mma::BM + mma::BM + mma::KMAX + 8) * 4;
@@ -50,7 +50,7 @@ int launch_mmaw_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bia
   const int64_t cap = static_cast<int64_t>(sm_count()) * occ;
   dim3 grid(static_cast<unsigned>(row_tiles < cap ? row_tiles : cap), static_cast<unsigned>(ceil_div(c_out, TN)));
   TSC_LAUNCH_PDL("k_conv_mmaw", kern, grid, dim3(mma::NT), smem, stream, f, n_in, c_in, w, bias, gmap, perm, K,
-                 n_out, c_out, ovf, ovf_cap, meta, out, flags, status);
+                 n_out, c_out, ovf, ovf_cap, meta, out, flags, epi, status);
   return TSC_OK;
 }
 
@@ -58,7 +58,7 @@ int launch_mmaw_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bia
 template <typename T, int TN, int KC, int CH, int RB>
 int launch_mma_rows(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                     const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                    const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+                    const int64_t* meta, T* out, int flags, const EpiParams& epi, int64_t* status, cudaStream_t stream) {
   using C = mma::Cfg<TN, KC, RB>;
   auto kern = mma::k_conv_mma<T, TN, KC, CH, RB>;
   static unsigned long long configured = 0;  // one bit per device
@@ -70,18 +70,18 @@ int launch_mma_rows(const T* f, int64_t n_in, int c_in, const T* w, const T* bia
   }
   dim3 grid(static_cast<unsigned>(ceil_div(n_out, RB)), static_cast<unsigned>(ceil_div(c_out, TN)));
   TSC_LAUNCH_PDL("k_conv_mma", kern, grid, dim3(mma::NT), C::bytes(K), stream, f, n_in, c_in, w, bias, gmap, perm,
-                 K, n_out, c_out, ovf, ovf_cap, meta, out, flags, status);
+                 K, n_out, c_out, ovf, ovf_cap, meta, out, flags, epi, status);
   return TSC_OK;
 }
 
 template <typename T, int TN, int KC, int CH>
 int launch_mma_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                    const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                   const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+                   const int64_t* meta, T* out, int flags, const EpiParams& epi, int64_t* status, cudaStream_t stream) {
   if ((flags & TSC_CONV_NO_RESIDENT_W) == 0 && c_in <= KC && K <= mma::KMAX &&
       static_cast<int64_t>(K) * TN * KC * 2 <= mma::kMaxResidentWeightBytes)
     return launch_mmaw_cfg<T, TN, KC, CH>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
-                                          out, flags, status, stream);
+                                          out, flags, epi, status, stream);
   // 16-channel chunks with narrow column tiles take 2 * BM rows per CTA (each
   // weight slice then serves twice the rows).  Measured on the config-3 maps:
   // 16->32 71.0 -> 68.5 us; 32-channel layers got slower (32->32 102 -> 113
@@ -89,10 +89,10 @@ int launch_mma_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias
   if constexpr (KC == 16 && TN <= 32) {
     if (n_out >= 4096)
       return launch_mma_rows<T, TN, KC, CH, 2 * mma::BM>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf,
-                                                         ovf_cap, meta, out, flags, status, stream);
+                                                         ovf_cap, meta, out, flags, epi, status, stream);
   }
   return launch_mma_rows<T, TN, KC, CH, mma::BM>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap,
-                                                 meta, out, flags, status, stream);
+                                                 meta, out, flags, epi, status, stream);
 }
 
 // ---- tcgen05 path ------------------------------------------------------------
@@ -100,7 +100,7 @@ int launch_mma_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias
 template <typename T, int TN, int KC>
 int launch_tc_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                   const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                  const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+                  const int64_t* meta, T* out, int flags, const EpiParams& epi, int64_t* status, cudaStream_t stream) {
   using C = tc::Cfg<TN, KC>;
   auto kern = tc::k_conv_tc<T, TN, KC>;
   const int smem = C::TOTAL_FIXED + K * tc::BM * 4;
@@ -114,7 +114,7 @@ int launch_tc_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias,
   }
   dim3 grid(static_cast<unsigned>(ceil_div(n_out, tc::BM)), static_cast<unsigned>(ceil_div(c_out, TN)));
   kern<<<grid, tc::NT, smem, stream>>>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
-                                       out, flags, status);
+                                       out, flags, epi, status);
   TSC_LAUNCH_CHECK("k_conv_tc");
   return TSC_OK;
 }
@@ -122,15 +122,15 @@ int launch_tc_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias,
 template <typename T, int TN>
 int launch_tc_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                  const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                 const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+                 const int64_t* meta, T* out, int flags, const EpiParams& epi, int64_t* status, cudaStream_t stream) {
   if (c_in <= 16)
     return launch_tc_cfg<T, TN, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                    flags, status, stream);
+                                    flags, epi, status, stream);
   if (c_in <= 32)
     return launch_tc_cfg<T, TN, 32>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                    flags, status, stream);
+                                    flags, epi, status, stream);
   return launch_tc_cfg<T, TN, 64>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                  flags, status, stream);
+                                  flags, epi, status, stream);
 }
 
 // ---- persistent tcgen05 path ---------------------------------------------------
@@ -207,7 +207,7 @@ int encode_maps(const T* f, int64_t n_in, int c_in, const T* w, int K, int c_out
 template <typename T, int TN, int KC>
 int launch_tcp_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                    const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                   const int64_t* meta, T* out, int flags, int64_t* status, uint32_t* tile_counter,
+                   const int64_t* meta, T* out, int flags, const EpiParams& epi, int64_t* status, uint32_t* tile_counter,
                    cudaStream_t stream) {
   using C = tcp::Cfg<TN, KC>;
   auto kern = tcp::k_conv_tcp<T, TN, KC>;
@@ -228,7 +228,7 @@ int launch_tcp_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias
     if (rc != TSC_OK) return rc;
   }
   TSC_LAUNCH_PDL("k_conv_tcp", kern, dim3(static_cast<unsigned>(grid)), dim3(tcp::NT), C::TOTAL, stream, mf, mw, f,
-                 n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out, flags, status,
+                 n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out, flags, epi, status,
                  tile_counter);
   return TSC_OK;
 }
@@ -236,17 +236,17 @@ int launch_tcp_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias
 template <typename T, int TN>
 int launch_tcp_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                   const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                  const int64_t* meta, T* out, int flags, int64_t* status, uint32_t* tile_counter,
+                  const int64_t* meta, T* out, int flags, const EpiParams& epi, int64_t* status, uint32_t* tile_counter,
                    cudaStream_t stream) {
   // KC = 64 divides c_in (tcp_eligible): every feature and weight box lies inside its tensor
   return launch_tcp_cfg<T, TN, 64>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                   flags, status, tile_counter, stream);
+                                   flags, epi, status, tile_counter, stream);
 }
 
 template <typename T>
 int launch_tcp(const void* F, int64_t n_in, int c_in, const void* W, const void* bias, const int32_t* gmap,
                const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-               const int64_t* meta, void* out, int flags, int64_t* status, uint32_t* tile_counter,
+               const int64_t* meta, void* out, int flags, const EpiParams& epi, int64_t* status, uint32_t* tile_counter,
                cudaStream_t stream) {
   const T* f = static_cast<const T*>(F);
   const T* w = static_cast<const T*>(W);
@@ -254,15 +254,15 @@ int launch_tcp(const void* F, int64_t n_in, int c_in, const void* W, const void*
   T* o = static_cast<T*>(out);
   // the largest UMMA N that divides c_out (tcp_eligible: c_out % 32 == 0)
   if (c_out % 256 == 0)
-    return launch_tcp_tn<T, 256>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+    return launch_tcp_tn<T, 256>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                                  status, tile_counter, stream);
   if (c_out % 128 == 0)
-    return launch_tcp_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+    return launch_tcp_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                                  status, tile_counter, stream);
   if (c_out % 64 == 0)
-    return launch_tcp_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+    return launch_tcp_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                                  status, tile_counter, stream);
-  return launch_tcp_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+  return launch_tcp_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                                  status, tile_counter, stream);
 }
 
@@ -290,7 +290,7 @@ int launch_tmh_tn(const ConvArgs& a) {
   const int64_t grid = tiles < sm_count() ? tiles : sm_count();
   TSC_LAUNCH_PDL("k_conv_tmh", kern, dim3(static_cast<unsigned>(grid)), dim3(tmh::NT), C::TOTAL, a.stream, mf, mw, f,
                  a.n_in, static_cast<const T*>(a.bias), a.gather_map, a.n_out, a.halo_rows, a.halo_count,
-                 a.plane_kmask, a.halo_map, a.halo_capacity, static_cast<T*>(a.out), a.flags, a.status);
+                 a.plane_kmask, a.halo_map, a.halo_capacity, static_cast<T*>(a.out), a.flags, a.epi, a.status);
   return TSC_OK;
 }
 
@@ -317,61 +317,61 @@ int launch_tmh(const ConvArgs& a) {
 template <typename T>
 int launch_tc(const void* F, int64_t n_in, int c_in, const void* W, const void* bias, const int32_t* gmap,
               const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-              const int64_t* meta, void* out, int flags, int64_t* status, cudaStream_t stream) {
+              const int64_t* meta, void* out, int flags, const EpiParams& epi, int64_t* status, cudaStream_t stream) {
   const T* f = static_cast<const T*>(F);
   const T* w = static_cast<const T*>(W);
   const T* b = static_cast<const T*>(bias);
   T* o = static_cast<T*>(out);
   if (c_out <= 32)
-    return launch_tc_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+    return launch_tc_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                                status, stream);
   if (c_out <= 64)
-    return launch_tc_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+    return launch_tc_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                                status, stream);
   if (c_out <= 128)
-    return launch_tc_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+    return launch_tc_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                                 status, stream);
-  return launch_tc_tn<T, 256>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+  return launch_tc_tn<T, 256>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                               status, stream);
 }
 
 template <typename T, int TN>
 int launch_mma_tn(const T* f, int64_t n_in, int c_in, const T* w, const T* bias, const int32_t* gmap,
                   const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-                  const int64_t* meta, T* out, int flags, int64_t* status, cudaStream_t stream) {
+                  const int64_t* meta, T* out, int flags, const EpiParams& epi, int64_t* status, cudaStream_t stream) {
   if (c_in <= 16) {
     if (c_in % 8 == 0)
       return launch_mma_cfg<T, TN, 16, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
-                                           out, flags, status, stream);
+                                           out, flags, epi, status, stream);
     return launch_mma_cfg<T, TN, 16, 8>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
-                                        out, flags, status, stream);
+                                        out, flags, epi, status, stream);
   }
   if (c_in <= 32)
     return launch_mma_cfg<T, TN, 32, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta,
-                                         out, flags, status, stream);
+                                         out, flags, epi, status, stream);
   return launch_mma_cfg<T, TN, 64, 16>(f, n_in, c_in, w, bias, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, out,
-                                       flags, status, stream);
+                                       flags, epi, status, stream);
 }
 
 
 template <typename T>
 int launch_mma(const void* F, int64_t n_in, int c_in, const void* W, const void* bias, const int32_t* gmap,
                const int32_t* perm, int K, int64_t n_out, int c_out, const int32_t* ovf, int64_t ovf_cap,
-               const int64_t* meta, void* out, int flags, int64_t* status, cudaStream_t stream) {
+               const int64_t* meta, void* out, int flags, const EpiParams& epi, int64_t* status, cudaStream_t stream) {
   const T* f = static_cast<const T*>(F);
   const T* w = static_cast<const T*>(W);
   const T* b = static_cast<const T*>(bias);
   T* o = static_cast<T*>(out);
   if (c_out <= 16)
-    return launch_mma_tn<T, 16>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+    return launch_mma_tn<T, 16>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                                 status, stream);
   if (c_out <= 32)
-    return launch_mma_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+    return launch_mma_tn<T, 32>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                                 status, stream);
   if (c_out <= 64)
-    return launch_mma_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+    return launch_mma_tn<T, 64>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                                 status, stream);
-  return launch_mma_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags,
+  return launch_mma_tn<T, 128>(f, n_in, c_in, w, b, gmap, perm, K, n_out, c_out, ovf, ovf_cap, meta, o, flags, epi,
                                status, stream);
 }
 

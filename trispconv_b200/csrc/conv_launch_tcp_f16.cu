@@ -5,7 +5,7 @@ namespace tsc {
 
 int launch_tcp_f16(const ConvArgs& a) {
   return detail::launch_tcp<__half>(a.features, a.n_in, a.c_in, a.weight, a.bias, a.gather_map, a.row_order,
-                                     a.k_vol, a.n_out, a.c_out, a.overflow, a.overflow_cap, a.meta, a.out, a.flags,
+                                     a.k_vol, a.n_out, a.c_out, a.overflow, a.overflow_cap, a.meta, a.out, a.flags, a.epi,
                                      a.status, a.tile_counter, a.stream);
 }
 

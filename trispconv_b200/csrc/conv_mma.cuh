@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(NT)
 k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__ W,
            const T* __restrict__ bias, const int32_t* __restrict__ gmap, const int32_t* __restrict__ perm,
            int K, int64_t n_out, int c_out, const int32_t* __restrict__ ovf, int64_t ovf_cap,
-           const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status) {
+           const int64_t* __restrict__ meta, T* __restrict__ out, int flags, EpiParams epi, int64_t* __restrict__ status) {
   pdl_wait();
   pdl_trigger();
   using C = Cfg<TN, KC, RB>;
@@ -305,7 +305,6 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
     }
   }
 
-  const bool relu = (flags & TSC_CONV_RELU) != 0;
   constexpr int CPR_OUT = TN / 8;  // 16-byte output chunks per row
   for (int u = tid; u < RB * CPR_OUT; u += NT) {
     const int r = u / CPR_OUT;
@@ -320,10 +319,7 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
     } pk;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      float v = src[i];
-      if (bias != nullptr) v += to_f32(bias[n + i]);
-      if (relu) v = fmaxf(v, 0.f);
-      pk.h[i] = from_f32<T>(v);
+      pk.h[i] = from_f32<T>(epi_apply(src[i], n + i, epi, bias));
     }
     *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o) * c_out + n) = pk.v;
   }
@@ -360,7 +356,7 @@ __global__ void __launch_bounds__(NT)
 k_conv_mmaw(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__ W,
             const T* __restrict__ bias, const int32_t* __restrict__ gmap, const int32_t* __restrict__ perm,
             int K, int64_t n_out, int c_out, const int32_t* __restrict__ ovf, int64_t ovf_cap,
-            const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status) {
+            const int64_t* __restrict__ meta, T* __restrict__ out, int flags, EpiParams epi, int64_t* __restrict__ status) {
   pdl_wait();
   pdl_trigger();
   using C = CfgW<TN, KC>;
@@ -385,7 +381,6 @@ k_conv_mmaw(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict
   const int warp = tid >> 5;
   const int n0 = blockIdx.y * TN;
   const int64_t n_row_tiles = (n_out + BM - 1) / BM;
-  const bool relu = (flags & TSC_CONV_RELU) != 0;
 
   // ---- resident weights: W[n0 + nn, k, 0:c_in] for all k --------------------
   for (int u = tid; u < K * TN * UPR; u += NT) {
@@ -568,10 +563,7 @@ k_conv_mmaw(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict
       } pk;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        float v = src[i];
-        if (bias != nullptr) v += to_f32(bias[n + i]);
-        if (relu) v = fmaxf(v, 0.f);
-        pk.h[i] = from_f32<T>(v);
+        pk.h[i] = from_f32<T>(epi_apply(src[i], n + i, epi, bias));
       }
       *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o) * c_out + n) = pk.v;
     }

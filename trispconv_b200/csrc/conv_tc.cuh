@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(NT, 1)
 k_conv_tc(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__ W,
           const T* __restrict__ bias, const int32_t* __restrict__ gmap, const int32_t* __restrict__ perm, int K,
           int64_t n_out, int c_out, const int32_t* __restrict__ ovf, int64_t ovf_cap,
-          const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status) {
+          const int64_t* __restrict__ meta, T* __restrict__ out, int flags, EpiParams epi, int64_t* __restrict__ status) {
   using C = Cfg<TN, KC>;
   constexpr int NS = C::NS;
   constexpr int UPR = KC * 2 / 16;  // 16-byte chunks per shared-memory row
@@ -374,7 +374,6 @@ k_conv_tc(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__
     tc_fence_after();
     const int r = tid;
     const int o = s_orow[r];
-    const bool relu = (flags & TSC_CONV_RELU) != 0;
     int64_t n_ovf = 0;
     if (ovf != nullptr && meta != nullptr) {
       n_ovf = static_cast<int64_t>(__ldg(&meta[TSC_META_N_OVERFLOW]));
@@ -420,12 +419,7 @@ k_conv_tc(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__
           T h[8];
         } pk;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float x = v[q * 8 + i];
-          if (bias != nullptr) x += to_f32(bias[n + i]);
-          if (relu) x = fmaxf(x, 0.f);
-          pk.h[i] = from_f32<T>(x);
-        }
+        for (int i = 0; i < 8; ++i) pk.h[i] = from_f32<T>(epi_apply(v[q * 8 + i], n + i, epi, bias));
         *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o) * c_out + n) = pk.u;
       }
     }

@@ -129,7 +129,7 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
            const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__ W,
            const T* __restrict__ bias, const int32_t* __restrict__ gmap, const int32_t* __restrict__ perm, int K,
            int64_t n_out, int c_out, const int32_t* __restrict__ ovf, int64_t ovf_cap,
-           const int64_t* __restrict__ meta, T* __restrict__ out, int flags, int64_t* __restrict__ status,
+           const int64_t* __restrict__ meta, T* __restrict__ out, int flags, EpiParams epi, int64_t* __restrict__ status,
            unsigned* __restrict__ tile_counter) {
   pdl_wait();
   pdl_trigger();
@@ -335,17 +335,20 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
     // ========================== epilogue and tile set-up ==========================
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int lrow = q * 32 + lane;
-    const bool relu = (flags & TSC_CONV_RELU) != 0;
     int64_t n_ovf = 0;
     if (ovf != nullptr && meta != nullptr) {
       n_ovf = static_cast<int64_t>(__ldg(&meta[TSC_META_N_OVERFLOW]));
       if (n_ovf > ovf_cap) n_ovf = ovf_cap;
     }
-    // one column tile: the bias is the same for every tile -> shared memory
+    // one column tile: the additive term of the store (bias, or the
+    // epilogue's shift) is the same for every tile -> shared memory
     const bool bias_smem = n_col_tiles == 1;
     if (bias_smem) {
       for (int i = tid - EPI0; i < TN; i += NEPI)
-        s_bias[i] = (bias != nullptr && i < c_out) ? to_f32(__ldg(&bias[i])) : 0.f;
+        s_bias[i] = i >= c_out                ? 0.f
+                    : epi.scale != nullptr ? __ldg(&epi.shift[i])
+                    : bias != nullptr      ? to_f32(__ldg(&bias[i]))
+                                           : 0.f;
       asm volatile("bar.sync 2, %0;" ::"r"(NEPI) : "memory");
     }
 
@@ -495,11 +498,12 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               float x = v[qq * 8 + i];
-              if (bias_smem)
-                x += s_bias[n + i];
-              else if (bias != nullptr)
-                x += to_f32(__ldg(&bias[n + i]));
-              if (relu) x = fmaxf(x, 0.f);
+              if (!bias_smem)
+                x = epi_apply(x, n + i, epi, bias);
+              else
+                x = activate(epi.scale != nullptr ? fmaf(x, __ldg(&epi.scale[n + i]), s_bias[n + i])
+                                                  : x + s_bias[n + i],
+                             epi.act, epi.alpha);
               pk.hv[i] = from_f32<T>(x);
             }
             *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o) * c_out + n) = pk.u;

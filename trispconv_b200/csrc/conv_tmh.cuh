@@ -158,7 +158,7 @@ k_conv_tmh(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
            const T* __restrict__ F, int64_t n_in, const T* __restrict__ bias, const int32_t* __restrict__ gmap,
            int64_t n_out, const int32_t* __restrict__ halo_rows, const int32_t* __restrict__ halo_count,
            const uint32_t* __restrict__ plane_kmask, const int16_t* __restrict__ hmap, int cap,
-           T* __restrict__ out, int flags, int64_t* __restrict__ status) {
+           T* __restrict__ out, int flags, EpiParams epi, int64_t* __restrict__ status) {
   pdl_wait();
   pdl_trigger();
   using C = Cfg<TN, NS_>;
@@ -205,7 +205,8 @@ k_conv_tmh(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp >= W_EPI0 && warp < W_ASM0) {
-    for (int i = tid - W_EPI0 * 32; i < TN; i += 4 * 32) s_bias[i] = bias != nullptr ? to_f32(__ldg(&bias[i])) : 0.f;
+    for (int i = tid - W_EPI0 * 32; i < TN; i += 4 * 32)
+      s_bias[i] = epi.scale != nullptr ? __ldg(&epi.shift[i]) : bias != nullptr ? to_f32(__ldg(&bias[i])) : 0.f;
   }
   if (warp == W_MMA) {
     __syncwarp();
@@ -295,7 +296,6 @@ k_conv_tmh(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
     const int q = warp & 3;
     const int lrow = q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    const bool relu = (flags & TSC_CONV_RELU) != 0;
     // both accumulator buffers start at zero (the MMAs always accumulate)
     for (int b = 0; b < C::NACC; ++b)
 #pragma unroll 1
@@ -331,9 +331,10 @@ k_conv_tmh(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
             } pk;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              float x = v[qq * 8 + i] + s_bias[c0 + qq * 8 + i];
-              if (relu) x = fmaxf(x, 0.f);
-              pk.hv[i] = from_f32<T>(x);
+              const int n = c0 + qq * 8 + i;
+              const float x = epi.scale != nullptr ? fmaf(v[qq * 8 + i], __ldg(&epi.scale[n]), s_bias[n])
+                                                   : v[qq * 8 + i] + s_bias[n];
+              pk.hv[i] = from_f32<T>(activate(x, epi.act, epi.alpha));
             }
             *reinterpret_cast<uint4*>(out + o * TN + c0 + qq * 8) = pk.u;
           }

@@ -1418,3 +1418,356 @@ int tsc_subm_kmap_noalloc(const int32_t* indices, int64_t n, const tsc_geometry*
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Voxelisation: points -> unique voxels in (b, z, y, x) key order
+// ---------------------------------------------------------------------------
+
+namespace tsc {
+namespace {
+
+struct VoxDev {
+  int B, D, H, W;
+  float lo[3];
+  float size[3];
+};
+
+VoxDev to_vox(const tsc_voxel_params& p) {
+  VoxDev v;
+  v.B = p.batch;
+  v.D = p.grid[0];
+  v.H = p.grid[1];
+  v.W = p.grid[2];
+  for (int d = 0; d < 3; ++d) {
+    v.lo[d] = p.range_lo[d];
+    v.size[d] = p.voxel_size[d];
+  }
+  return v;
+}
+
+// Voxel (b, z, y, x) of point i; false when it lies outside the grid (NaN
+// coordinates included) or its batch id is outside [0, B) (then *bad).
+__device__ __forceinline__ bool point_voxel(const float* __restrict__ pts, int dim, const int32_t* __restrict__ bid,
+                                            int64_t i, const VoxDev& v, int& b, int& z, int& y, int& x, bool& bad) {
+  b = bid != nullptr ? __ldg(&bid[i]) : 0;
+  bad = b < 0 || b >= v.B;
+  if (bad) return false;
+  const float* p = pts + i * dim;
+  const float fx = floorf((__ldg(&p[0]) - v.lo[0]) / v.size[0]);
+  const float fy = floorf((__ldg(&p[1]) - v.lo[1]) / v.size[1]);
+  const float fz = floorf((__ldg(&p[2]) - v.lo[2]) / v.size[2]);
+  if (!(fx >= 0.f && fx < static_cast<float>(v.W) && fy >= 0.f && fy < static_cast<float>(v.H) && fz >= 0.f &&
+        fz < static_cast<float>(v.D)))
+    return false;
+  x = static_cast<int>(fx);
+  y = static_cast<int>(fy);
+  z = static_cast<int>(fz);
+  return x < v.W && y < v.H && z < v.D;
+}
+
+template <typename KeyT>
+__global__ void __launch_bounds__(kThreads)
+k_vox_mark(const float* __restrict__ pts, int64_t n, int dim, const int32_t* __restrict__ bid, VoxDev v,
+           uint32_t* __restrict__ bitmap, unsigned long long* __restrict__ meta, int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  int b = 0, z = 0, y = 0, x = 0;
+  bool bad = false;
+  const bool ok = i < n && point_voxel(pts, dim, bid, i, v, b, z, y, x, bad);
+  if (i < n && bad) raise_status(status, TSC_STATUS_KEY_RANGE);
+  const unsigned kept = __ballot_sync(kFullMask, ok);
+  if (ok) {
+    // lanes that hit the same bitmap word combine their bits; one atomic per word
+    const KeyT lin = cell_key_t<KeyT>(b, z, y, x, v.D, v.H, v.W);
+    const KeyT word = lin >> 5;
+    const unsigned same = __match_any_sync(kept, word);
+    const unsigned bits = __reduce_or_sync(same, 1u << static_cast<unsigned>(lin & 31u));
+    if ((threadIdx.x & 31) == static_cast<unsigned>(__ffs(same) - 1)) atomicOr(&bitmap[word], bits);
+  }
+  if ((threadIdx.x & 31) == 0 && kept) atomicAdd(&meta[TSC_META_N_PART], static_cast<unsigned long long>(__popc(kept)));
+}
+
+// Voxel rank of every kept point (-1 for dropped ones) and the points per voxel.
+template <typename KeyT>
+__global__ void __launch_bounds__(kThreads)
+k_vox_rank(const float* __restrict__ pts, int64_t n, int dim, const int32_t* __restrict__ bid, VoxDev v,
+           const uint32_t* __restrict__ bitmap, const uint32_t* __restrict__ word_prefix, int64_t n_vox,
+           int32_t* __restrict__ rank, int32_t* __restrict__ counts, int64_t* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int b = 0, z = 0, y = 0, x = 0;
+  bool bad = false;
+  int r = -1;
+  if (point_voxel(pts, dim, bid, i, v, b, z, y, x, bad)) {
+    const KeyT lin = cell_key_t<KeyT>(b, z, y, x, v.D, v.H, v.W);
+    const KeyT w = lin >> 5;
+    r = static_cast<int>(__ldg(&word_prefix[w]) +
+                         __popc(__ldg(&bitmap[w]) & ((1u << static_cast<unsigned>(lin & 31u)) - 1u)));
+    if (r >= n_vox) {
+      raise_status(status, TSC_STATUS_INTERNAL);
+      r = -1;
+    } else {
+      atomicAdd(&counts[r], 1);
+    }
+  }
+  rank[i] = r;
+}
+
+// Exclusive prefix of per-voxel counts: tile sums, then per element.
+__global__ void __launch_bounds__(kThreads)
+k_vox_tile_sums(const int32_t* __restrict__ counts, int64_t n, uint32_t* __restrict__ tile_sums) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ uint32_t ws[32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j)
+    if (base + j < n) s += static_cast<uint32_t>(counts[base + j]);
+  uint32_t total;
+  block_exclusive_scan(s, ws, &total);
+  if (threadIdx.x == 0) tile_sums[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_vox_offsets(const int32_t* __restrict__ counts, int64_t n, const uint32_t* __restrict__ tile_off,
+              int32_t* __restrict__ offsets) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ uint32_t ws[32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile + threadIdx.x * kItems;
+  uint32_t c[kItems];
+  uint32_t s = 0;
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    c[j] = base + j < n ? static_cast<uint32_t>(counts[base + j]) : 0u;
+    s += c[j];
+  }
+  uint32_t total;
+  uint32_t run = block_exclusive_scan(s, ws, &total) + tile_off[blockIdx.x];
+#pragma unroll
+  for (int j = 0; j < kItems; ++j) {
+    if (base + j < n) offsets[base + j] = static_cast<int32_t>(run);
+    run += c[j];
+  }
+}
+
+// Every kept point into its voxel's segment of `list` (order within the
+// segment depends on the atomics; k_vox_reduce sorts it).
+__global__ void __launch_bounds__(kThreads)
+k_vox_fill(const int32_t* __restrict__ rank, int64_t n, const int32_t* __restrict__ offsets,
+           int32_t* __restrict__ fill, int32_t* __restrict__ list) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int r = rank[i];
+  if (r < 0) return;
+  const int slot = atomicAdd(&fill[r], 1);
+  list[offsets[r] + slot] = static_cast<int32_t>(i);
+}
+
+// One thread per voxel: sort its point indices ascending (insertion sort:
+// voxels hold few points), keep the first max_points, and average every
+// column over them, summing in index order.
+__global__ void __launch_bounds__(kThreads)
+k_vox_reduce(const float* __restrict__ pts, int dim, int32_t* __restrict__ list, const int32_t* __restrict__ offsets,
+             const int32_t* __restrict__ counts, int64_t n_vox, int max_points, float* __restrict__ features,
+             int32_t* __restrict__ num_points) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (v >= n_vox) return;
+  const int c = counts[v];
+  int32_t* seg = list + offsets[v];
+  for (int a = 1; a < c; ++a) {
+    const int32_t key = seg[a];
+    int j = a - 1;
+    while (j >= 0 && seg[j] > key) {
+      seg[j + 1] = seg[j];
+      --j;
+    }
+    seg[j + 1] = key;
+  }
+  const int m = (max_points > 0 && c > max_points) ? max_points : c;
+  num_points[v] = m;
+  for (int d = 0; d < dim; ++d) {
+    float s = 0.f;
+    for (int a = 0; a < m; ++a) s += __ldg(&pts[static_cast<int64_t>(seg[a]) * dim + d]);
+    features[v * dim + d] = m > 0 ? s / static_cast<float>(m) : 0.f;
+  }
+}
+
+struct VoxWs {
+  StridedWs bm;  // occupancy bitmap, word prefix, tile sums over batch*D*H*W
+  size_t off_rank, off_counts, off_offsets, off_fill, off_list, off_vsums, bytes;
+  int64_t vtiles;
+};
+
+VoxWs vox_ws(const tsc_voxel_params& p, int64_t n) {
+  tsc_geometry g{};
+  g.batch = p.batch;
+  for (int d = 0; d < 3; ++d) g.out_shape[d] = p.grid[d];
+  VoxWs w;
+  w.bm = strided_ws(g);
+  const size_t nn = static_cast<size_t>(n < 1 ? 1 : n);
+  w.vtiles = ceil_div(static_cast<int64_t>(nn), kTile);
+  w.off_rank = align_up(w.bm.bytes, 256);
+  w.off_counts = w.off_rank + align_up(nn * 4, 256);
+  w.off_offsets = w.off_counts + align_up(nn * 4, 256);
+  w.off_fill = w.off_offsets + align_up(nn * 4, 256);
+  w.off_list = w.off_fill + align_up(nn * 4, 256);
+  w.off_vsums = w.off_list + align_up(nn * 4, 256);
+  w.bytes = w.off_vsums + align_up(static_cast<size_t>(w.vtiles + 1) * 4, 256);
+  return w;
+}
+
+int check_vox(const float* points, int64_t n, int32_t dim, const tsc_voxel_params* vp, int64_t* meta,
+              int64_t* status) {
+  TSC_CHECK_ARG(vp != nullptr, "voxel parameters are NULL");
+  TSC_CHECK_ARG(vp->batch > 0 && vp->grid[0] > 0 && vp->grid[1] > 0 && vp->grid[2] > 0,
+                "batch and grid extents must be positive");
+  for (int d = 0; d < 3; ++d)
+    TSC_CHECK_ARG(vp->voxel_size[d] > 0.f, "voxel_size[%d] must be positive", d);
+  TSC_CHECK_ARG(dim >= 3 && dim <= 64, "point_dim %d must be in [3, 64]", dim);
+  TSC_CHECK_ARG(n >= 0 && n <= 0x7fffffffLL, "number of points %lld out of range", (long long)n);
+  TSC_CHECK_ARG(n == 0 || (points != nullptr && aligned(points, 4)), "points must not be NULL");
+  TSC_CHECK_ARG(meta != nullptr && status != nullptr, "meta/status must not be NULL");
+  tsc_geometry g{};
+  g.batch = vp->batch;
+  for (int d = 0; d < 3; ++d) g.out_shape[d] = vp->grid[d];
+  if (cells_of(g.batch, g.out_shape) > kMaxCells64) {
+    set_error("voxel grid batch*D*H*W exceeds 2^62 cells");
+    return TSC_ERR_GRID_TOO_LARGE;
+  }
+  return TSC_OK;
+}
+
+}  // namespace
+}  // namespace tsc
+
+extern "C" {
+
+size_t tsc_voxelize_workspace(const tsc_voxel_params* vp, int64_t n_points) {
+  if (vp == nullptr || vp->batch <= 0 || vp->grid[0] <= 0 || vp->grid[1] <= 0 || vp->grid[2] <= 0) return 0;
+  tsc_geometry g{};
+  g.batch = vp->batch;
+  for (int d = 0; d < 3; ++d) g.out_shape[d] = vp->grid[d];
+  if (cells_of(g.batch, g.out_shape) > kMaxCells64) return 0;
+  return vox_ws(*vp, n_points).bytes;
+}
+
+int tsc_voxelize_count(const float* points, int64_t n, int32_t point_dim, const int32_t* batch_ids,
+                       const tsc_voxel_params* vp, void* workspace, size_t workspace_bytes, int64_t* meta,
+                       int64_t* status, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int rc = check_vox(points, n, point_dim, vp, meta, status);
+  if (rc != TSC_OK) return rc;
+  const VoxWs w = vox_ws(*vp, n);
+  if (workspace == nullptr || workspace_bytes < w.bytes || !aligned(workspace, 256)) {
+    set_error("voxelize workspace needs %zu bytes (256-byte aligned), got %zu", w.bytes, workspace_bytes);
+    return TSC_ERR_WORKSPACE;
+  }
+  char* ws = static_cast<char*>(workspace);
+  auto* bitmap = reinterpret_cast<uint32_t*>(ws);
+  auto* sums = reinterpret_cast<uint32_t*>(ws + w.bm.off_sums);
+  auto* umeta = reinterpret_cast<unsigned long long*>(meta);
+  rc = fill_words(meta, 0u, 2 * static_cast<int64_t>(TSC_META_COUNTS), bitmap, 0u, w.bm.nwords_pad, stream);
+  if (rc != TSC_OK) return rc;
+  const VoxDev v = to_vox(*vp);
+  const bool wide = w.bm.nbits > kMaxCells;
+  if (n > 0) {
+    const unsigned grid = static_cast<unsigned>(ceil_div(n, kThreads));
+    if (wide)
+      TSC_LAUNCH_PDL("k_vox_mark", k_vox_mark<unsigned long long>, dim3(grid), dim3(kThreads), 0, stream, points, n,
+                     point_dim, batch_ids, v, bitmap, umeta, status);
+    else
+      TSC_LAUNCH_PDL("k_vox_mark", k_vox_mark<uint32_t>, dim3(grid), dim3(kThreads), 0, stream, points, n,
+                     point_dim, batch_ids, v, bitmap, umeta, status);
+  }
+  TSC_LAUNCH_PDL("k_bitmap_tile_count", k_bitmap_tile_count, dim3(static_cast<unsigned>(w.bm.nblocks)), dim3(kThreads),
+                 0, stream, reinterpret_cast<const uint4*>(bitmap), sums);
+  TSC_LAUNCH_PDL("k_scan_tile_sums", k_scan_tile_sums<uint32_t>, dim3(1), dim3(kScanBlockThreads), 0, stream, sums,
+                 w.bm.nblocks, umeta, TSC_META_N_OUT, static_cast<const int64_t*>(status),
+                 static_cast<unsigned long long*>(nullptr), 0);
+  return TSC_OK;
+}
+
+int tsc_voxelize_emit(const float* points, int64_t n, int32_t point_dim, const int32_t* batch_ids,
+                      const tsc_voxel_params* vp, void* workspace, size_t workspace_bytes, int64_t n_vox,
+                      int32_t* coords, float* features, int32_t* num_points, int64_t* meta, int64_t* status,
+                      void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int rc = check_vox(points, n, point_dim, vp, meta, status);
+  if (rc != TSC_OK) return rc;
+  TSC_CHECK_ARG(n_vox >= 0 && n_vox <= n, "n_vox %lld must lie in [0, n]", (long long)n_vox);
+  const VoxWs w = vox_ws(*vp, n);
+  if (workspace == nullptr || workspace_bytes < w.bytes || !aligned(workspace, 256)) {
+    set_error("voxelize workspace needs %zu bytes (256-byte aligned), got %zu", w.bytes, workspace_bytes);
+    return TSC_ERR_WORKSPACE;
+  }
+  if (n_vox == 0) return TSC_OK;
+  TSC_CHECK_ARG(coords != nullptr && aligned(coords, 16) && features != nullptr && num_points != nullptr,
+                "coords (16-byte aligned), features and num_points must not be NULL");
+  char* ws = static_cast<char*>(workspace);
+  auto* bitmap = reinterpret_cast<uint32_t*>(ws);
+  auto* prefix = reinterpret_cast<uint32_t*>(ws + w.bm.off_prefix);
+  auto* sums = reinterpret_cast<uint32_t*>(ws + w.bm.off_sums);
+  auto* rank = reinterpret_cast<int32_t*>(ws + w.off_rank);
+  auto* counts = reinterpret_cast<int32_t*>(ws + w.off_counts);
+  auto* offsets = reinterpret_cast<int32_t*>(ws + w.off_offsets);
+  auto* fill = reinterpret_cast<int32_t*>(ws + w.off_fill);
+  auto* list = reinterpret_cast<int32_t*>(ws + w.off_list);
+  auto* vsums = reinterpret_cast<uint32_t*>(ws + w.off_vsums);
+  const VoxDev v = to_vox(*vp);
+  const bool wide = w.bm.nbits > kMaxCells;
+  rc = fill_words(counts, 0u, n_vox, fill, 0u, n_vox, stream);
+  if (rc != TSC_OK) return rc;
+  TSC_LAUNCH_PDL("k_bitmap_prefix", k_bitmap_prefix, dim3(static_cast<unsigned>(w.bm.nblocks)), dim3(kThreads), 0,
+                 stream, reinterpret_cast<const uint4*>(bitmap), static_cast<const uint32_t*>(sums), prefix);
+  // voxel coordinates in key order: the bitmap decoded like a strided map's
+  // output set (B = batch, out grid = the voxel grid)
+  GeoDev g{};
+  g.B = v.B;
+  g.oD = v.D;
+  g.oH = v.H;
+  g.oW = v.W;
+  const int64_t nwords = static_cast<int64_t>((w.bm.nbits + 31) / 32);
+  const unsigned cgrid = static_cast<unsigned>(ceil_div(nwords, kThreads));
+  if (wide)
+    TSC_LAUNCH_PDL("k_bitmap_coords", k_bitmap_coords<unsigned long long>, dim3(cgrid), dim3(kThreads), 0, stream,
+                   static_cast<const uint32_t*>(bitmap), static_cast<const uint32_t*>(prefix), nwords, g,
+                   reinterpret_cast<int4*>(coords), n_vox);
+  else
+    TSC_LAUNCH_PDL("k_bitmap_coords", k_bitmap_coords<uint32_t>, dim3(cgrid), dim3(kThreads), 0, stream,
+                   static_cast<const uint32_t*>(bitmap), static_cast<const uint32_t*>(prefix), nwords, g,
+                   reinterpret_cast<int4*>(coords), n_vox);
+  const unsigned pgrid = static_cast<unsigned>(ceil_div(n, kThreads));
+  if (wide)
+    TSC_LAUNCH_PDL("k_vox_rank", k_vox_rank<unsigned long long>, dim3(pgrid), dim3(kThreads), 0, stream, points, n,
+                   point_dim, batch_ids, v, static_cast<const uint32_t*>(bitmap), static_cast<const uint32_t*>(prefix),
+                   n_vox, rank, counts, status);
+  else
+    TSC_LAUNCH_PDL("k_vox_rank", k_vox_rank<uint32_t>, dim3(pgrid), dim3(kThreads), 0, stream, points, n, point_dim,
+                   batch_ids, v, static_cast<const uint32_t*>(bitmap), static_cast<const uint32_t*>(prefix), n_vox,
+                   rank, counts, status);
+  const int64_t vt = ceil_div(n_vox, kTile);
+  TSC_LAUNCH_PDL("k_vox_tile_sums", k_vox_tile_sums, dim3(static_cast<unsigned>(vt)), dim3(kThreads), 0, stream,
+                 static_cast<const int32_t*>(counts), n_vox, vsums);
+  TSC_LAUNCH_PDL("k_scan_tile_sums", k_scan_tile_sums<uint32_t>, dim3(1), dim3(kScanBlockThreads), 0, stream, vsums,
+                 vt, static_cast<unsigned long long*>(nullptr), 0, static_cast<const int64_t*>(nullptr),
+                 static_cast<unsigned long long*>(nullptr), 0);
+  TSC_LAUNCH_PDL("k_vox_offsets", k_vox_offsets, dim3(static_cast<unsigned>(vt)), dim3(kThreads), 0, stream,
+                 static_cast<const int32_t*>(counts), n_vox, static_cast<const uint32_t*>(vsums), offsets);
+  TSC_LAUNCH_PDL("k_vox_fill", k_vox_fill, dim3(pgrid), dim3(kThreads), 0, stream, static_cast<const int32_t*>(rank),
+                 n, static_cast<const int32_t*>(offsets), fill, list);
+  TSC_LAUNCH_PDL("k_vox_reduce", k_vox_reduce, dim3(static_cast<unsigned>(ceil_div(n_vox, kThreads))), dim3(kThreads),
+                 0, stream, points, point_dim, list, static_cast<const int32_t*>(offsets),
+                 static_cast<const int32_t*>(counts), n_vox, vp->max_points, features, num_points);
+  return TSC_OK;
+}
+
+}  // extern "C"

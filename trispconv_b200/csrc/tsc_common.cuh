@@ -143,6 +143,36 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
   return __float2bfloat16_rn(v);
 }
 
+// ---- convolution epilogue ------------------------------------------------------
+// Per output channel n: out = act(acc * scale[n] + shift[n]) when scale is set
+// (an eval-mode BatchNorm folded into the store, the conv bias inside shift),
+// else act(acc + bias[n]).  Computed in fp32 and rounded once to the output
+// type.
+struct EpiParams {
+  const float* scale;
+  const float* shift;
+  int act;      // TSC_ACT_*
+  float alpha;  // negative slope of TSC_ACT_LEAKY_RELU
+};
+
+__device__ __forceinline__ float activate(float x, int act, float alpha) {
+  switch (act) {
+    case TSC_ACT_RELU: return fmaxf(x, 0.f);
+    case TSC_ACT_LEAKY_RELU: return x >= 0.f ? x : x * alpha;
+    case TSC_ACT_SILU: return x / (1.f + expf(-x));
+    default: return x;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float epi_apply(float v, int n, const EpiParams& e, const T* __restrict__ bias) {
+  if (e.scale != nullptr)
+    v = fmaf(v, __ldg(&e.scale[n]), __ldg(&e.shift[n]));
+  else if (bias != nullptr)
+    v += to_f32(bias[n]);
+  return activate(v, e.act, e.alpha);
+}
+
 // Block-wide exclusive scan of one uint32 per thread (blockDim.x multiple of 32,
 // at most 1024).  `warp_sums` must hold 32 entries.  Returns the exclusive prefix
 // and writes the block total to *total.

@@ -12,6 +12,7 @@ from trispconv_b200.pytorch.modules import (
     SubMConv3d,
 )
 from trispconv_b200.pytorch.tensor import SparseConvTensor
+from trispconv_b200.pytorch.voxelize import voxel_grid, voxelize
 
 __all__ = [
     "SparseConvTensor",
@@ -22,4 +23,6 @@ __all__ = [
     "SparseSequential",
     "SparseModule",
     "ConvAlgo",
+    "voxelize",
+    "voxel_grid",
 ]

@@ -101,11 +101,32 @@ def _as_dtype(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return L.aligned(t, 16)
 
 
+class Epilogue:
+    """What the convolution's store applies per output channel n: with
+    `scale`/`shift` (float32 [C_out] device tensors, the conv bias folded into
+    shift) out = act(acc * scale[n] + shift[n]), else act(acc + bias[n]).
+    act: one of _lib.ACT_* ; alpha: the LeakyReLU negative slope."""
+
+    __slots__ = ("scale", "shift", "act", "alpha")
+
+    def __init__(self, act: int = L.ACT_NONE, alpha: float = 0.0, scale: Optional[torch.Tensor] = None,
+                 shift: Optional[torch.Tensor] = None):
+        self.act = int(act)
+        self.alpha = float(alpha)
+        self.scale = scale
+        self.shift = shift
+
+
+RELU = Epilogue(L.ACT_RELU)
+
+
 def conv_launch(features: torch.Tensor, weight: torch.Tensor, weight_layout: int,
                 bias: Optional[torch.Tensor], km: Optional[KernelMap], n_out: int, c_out: int,
-                relu: bool = False) -> torch.Tensor:
-    """One tsc_conv_forward launch.  `weight` is (K, Cin, Cout) for W_KCC or
-    (Cout, kD, kH, kW, Cin) for W_KRSC; km None means the identity map."""
+                relu: bool = False, epilogue: Optional[Epilogue] = None) -> torch.Tensor:
+    """One tsc_conv_forward(_ex) launch.  `weight` is (K, Cin, Cout) for W_KCC
+    or (Cout, kD, kH, kW, Cin) for W_KRSC; km None means the identity map.
+    `relu` fuses a ReLU into the store; `epilogue` (an Epilogue) a folded
+    BatchNorm and/or another activation."""
     dev = features.device
     dtype = features.dtype
     n_in, c_in = features.shape
@@ -141,15 +162,27 @@ def conv_launch(features: torch.Tensor, weight: torch.Tensor, weight_layout: int
             halo = km.halo
             if halo is None or halo[0] != hcap:
                 halo = km.halo = build_tile_halo(km, hcap, n_in)
-    if halo is not None:
-        hcap, hrows, hcount, hkmask, hmap = halo
-        rc = lib.tsc_conv_forward_halo(feats.data_ptr(), L.DTYPE_CODE[dtype], n_in, c_in, w.data_ptr(),
-                                       weight_layout, L.ptr(b), gather.data_ptr(), None, k_vol, n_out, c_out,
-                                       L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(), flags,
-                                       L.status_word(dev).data_ptr(), counter.data_ptr(),
-                                       hrows.data_ptr(), hcount.data_ptr(), hkmask.data_ptr(), hmap.data_ptr(),
-                                       L.HALO_PLANES, hcap, stream)
-        L.check(rc, "tsc_conv_forward_halo")
+    if epilogue is not None and epilogue.act == L.ACT_RELU and epilogue.scale is None:
+        flags |= L.CONV_RELU
+        epilogue = None
+    if halo is not None or epilogue is not None:
+        ex = L.ConvExtras()
+        if epilogue is not None:
+            ex.act = epilogue.act
+            ex.act_alpha = epilogue.alpha
+            if epilogue.scale is not None:
+                ex.scale = epilogue.scale.data_ptr()
+                ex.shift = epilogue.shift.data_ptr()
+        if halo is not None:
+            hcap, hrows, hcount, hkmask, hmap = halo
+            ex.halo_rows, ex.halo_count = hrows.data_ptr(), hcount.data_ptr()
+            ex.plane_kmask, ex.halo_map = hkmask.data_ptr(), hmap.data_ptr()
+            ex.halo_planes, ex.halo_capacity = L.HALO_PLANES, hcap
+        rc = lib.tsc_conv_forward_ex(feats.data_ptr() if n_in else None, L.DTYPE_CODE[dtype], n_in, c_in,
+                                     w.data_ptr(), weight_layout, L.ptr(b), L.ptr(gather), L.ptr(order), k_vol,
+                                     n_out, c_out, L.ptr(overflow), cap, L.ptr(meta), out.data_ptr(), flags,
+                                     L.status_word(dev).data_ptr(), counter.data_ptr(), L.byref(ex), stream)
+        L.check(rc, "tsc_conv_forward_ex")
     else:
         rc = lib.tsc_conv_forward(feats.data_ptr() if n_in else None, L.DTYPE_CODE[dtype], n_in, c_in,
                                   w.data_ptr(), weight_layout, L.ptr(b), L.ptr(gather), L.ptr(order), k_vol, n_out,

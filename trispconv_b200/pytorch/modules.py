@@ -15,7 +15,7 @@ import torch
 import torch.nn as nn
 
 from trispconv_b200 import _lib as L
-from trispconv_b200.pytorch.functional import check_features, conv_launch, kernel_map_for
+from trispconv_b200.pytorch.functional import Epilogue, check_features, conv_launch, kernel_map_for
 from trispconv_b200.pytorch.indices import (
     IndiceData,
     PendingStrided,
@@ -104,7 +104,9 @@ class SparseConvolution(SparseModule):
             km = kernel_map_for(data, n_out, features.device)
         k_used = km.k_vol if km is not None else 1
         w, layout = self._kernel_weight(k_used)
-        return conv_launch(features, w, layout, self.bias, km, n_out, self.out_channels, relu=relu)
+        if isinstance(relu, Epilogue):  # a fused BatchNorm / activation (SparseSequential)
+            return conv_launch(features, w, layout, self.bias, km, n_out, self.out_channels, epilogue=relu)
+        return conv_launch(features, w, layout, self.bias, km, n_out, self.out_channels, relu=bool(relu))
 
     # -- forward ------------------------------------------------------------------
     def forward(self, x: SparseConvTensor) -> SparseConvTensor:
@@ -248,18 +250,58 @@ def _start_next_strided(mods, start: int, x: SparseConvTensor, pending: dict) ->
             return  # a sparse module of unknown effect on the coordinates
 
 
+def _no_hooks(m: nn.Module) -> bool:
+    return not m._forward_hooks and not m._forward_pre_hooks
+
+
 def _fusable(conv: nn.Module, act: nn.Module) -> bool:
     """conv followed by a plain ReLU, no hooks, no forward override."""
     return (FUSE_RELU and isinstance(conv, SparseConvolution) and type(act) is nn.ReLU
-            and type(conv).forward is SparseConvolution.forward
-            and not conv._forward_hooks and not conv._forward_pre_hooks
-            and not act._forward_hooks and not act._forward_pre_hooks)
+            and type(conv).forward is SparseConvolution.forward and _no_hooks(conv) and _no_hooks(act))
+
+
+_ACTS = {nn.ReLU: L.ACT_RELU, nn.LeakyReLU: L.ACT_LEAKY_RELU, nn.SiLU: L.ACT_SILU}
+
+
+def _foldable_bn(bn: nn.Module, conv: "SparseConvolution") -> bool:
+    """An eval-mode BatchNorm1d over the conv's output channels: a per-channel
+    affine map of the features, which the conv's store can apply."""
+    return (type(bn) is nn.BatchNorm1d and not bn.training and bn.track_running_stats
+            and bn.running_mean is not None and bn.running_var is not None
+            and bn.num_features == conv.out_channels and _no_hooks(bn))
+
+
+def _fold_bn(bn: nn.BatchNorm1d, conv: "SparseConvolution", device: torch.device):
+    """(scale, shift) float32 [C] with bn(conv + bias) == conv * scale + shift:
+    scale = gamma / sqrt(running_var + eps), shift = beta + (bias - mean) * scale."""
+    with torch.no_grad():
+        var = bn.running_var.to(device=device, dtype=torch.float32)
+        mean = bn.running_mean.to(device=device, dtype=torch.float32)
+        scale = torch.rsqrt(var + float(bn.eps))
+        if bn.affine and bn.weight is not None:
+            scale = scale * bn.weight.to(device=device, dtype=torch.float32)
+        b = conv.bias.to(device=device, dtype=torch.float32) if conv.bias is not None else torch.zeros_like(mean)
+        shift = (b - mean) * scale
+        if bn.affine and bn.bias is not None:
+            shift = shift + bn.bias.to(device=device, dtype=torch.float32)
+    return scale.contiguous(), shift.contiguous()
+
+
+def _fold_key(bn: nn.BatchNorm1d, conv: "SparseConvolution", device: torch.device):
+    """Changes whenever a tensor the fold reads is modified in place."""
+    parts = [device, float(bn.eps), bn.running_mean._version, bn.running_var._version, id(bn.running_mean),
+             id(bn.running_var)]
+    for t in (bn.weight, bn.bias, conv.bias):
+        parts += [None, None] if t is None else [id(t), t._version]
+    return tuple(parts)
 
 
 class SparseSequential(SparseModule):
     """Sequential container; dense modules (BN, ReLU, ...) get x.features
-    (modules.py:306-329).  A SparseConvolution directly followed by nn.ReLU
-    runs as one kernel with the ReLU applied in its store."""
+    (modules.py:306-329).  A SparseConvolution directly followed by an
+    eval-mode nn.BatchNorm1d and/or nn.ReLU / nn.LeakyReLU / nn.SiLU runs as
+    one kernel with the BatchNorm and activation applied in its store
+    (TRISPCONV_B200_FUSE=0 turns the fusion off)."""
 
     def __init__(self, *args, **kwargs):
         super().__init__()
@@ -271,6 +313,43 @@ class SparseSequential(SparseModule):
                 self.add_module(str(idx), module)
         for key, module in kwargs.items():
             self.add_module(key, module)
+
+    def _fusion(self, mods, i: int):
+        """(number of dense modules after mods[i] that its store takes over,
+        what it applies: True for a plain ReLU, else an Epilogue).  Fused are
+        an eval-mode BatchNorm1d (folded into a per-channel scale and shift)
+        and/or a following ReLU, LeakyReLU or SiLU; (0, False) when mods[i]
+        is not a plain SparseConvolution or nothing follows that fuses."""
+        conv = mods[i]
+        if not (FUSE_RELU and isinstance(conv, SparseConvolution) and type(conv).forward is SparseConvolution.forward
+                and _no_hooks(conv)):
+            return 0, False
+        j = i + 1
+        bn = None
+        if j < len(mods) and _foldable_bn(mods[j], conv):
+            bn = mods[j]
+            j += 1
+        act = L.ACT_NONE
+        alpha = 0.0
+        if j < len(mods) and type(mods[j]) in _ACTS and _no_hooks(mods[j]):
+            act = _ACTS[type(mods[j])]
+            alpha = float(mods[j].negative_slope) if act == L.ACT_LEAKY_RELU else 0.0
+            j += 1
+        if j == i + 1:
+            return 0, False
+        if bn is None and act == L.ACT_RELU:
+            return 1, True
+        epi = Epilogue(act, alpha)
+        if bn is not None:
+            dev = conv.weight.device
+            cache = self.__dict__.setdefault("_bn_folds", {})
+            key = _fold_key(bn, conv, dev)
+            hit = cache.get(id(bn))
+            if hit is None or hit[0] != key:
+                hit = (key, _fold_bn(bn, conv, dev))
+                cache[id(bn)] = hit
+            epi.scale, epi.shift = hit[1]
+        return j - i - 1, epi
 
     def __len__(self) -> int:
         return len(self._modules)
@@ -295,9 +374,10 @@ class SparseSequential(SparseModule):
                     with torch.no_grad():
                         _start_next_strided(mods, i, x, pending)
                     scanned = x.indices
-                if i + 1 < len(mods) and _fusable(module, mods[i + 1]):
-                    x = module._forward_impl(x, relu=True, pending=pending.pop(id(module), None))
-                    i += 2
+                n_post, post = self._fusion(mods, i)
+                if n_post:
+                    x = module._forward_impl(x, relu=post, pending=pending.pop(id(module), None))
+                    i += 1 + n_post
                     continue
                 if id(module) in pending and _plain_conv(module):
                     x = module._forward_impl(x, relu=False, pending=pending.pop(id(module)))
