@@ -139,6 +139,17 @@ TSC_API int tsc_subm_kmap_dense(const int32_t* indices, int64_t n, const tsc_geo
                   int32_t* table, int64_t table_cells,
                   int32_t* gather_map, int64_t* meta, int64_t* status, void* stream);
 
+/* Rank variant: the same map as tsc_subm_kmap for `indices` that are the
+ * output coordinates of a strided map over this grid (the out_indices of
+ * tsc_strided_kmap_emit, unchanged), taken from that map's workspace after
+ * its emit step: a cell's row is the rank of its bit in the occupancy
+ * bitmap, so no table is built or cleared.  geo is the submanifold geometry
+ * (in_shape == the strided map's out_shape, same batch); strided_workspace
+ * and workspace_bytes are that strided map's.  Any grid up to 2^62 cells. */
+TSC_API int tsc_subm_kmap_ranked(const int32_t* indices, int64_t n, const tsc_geometry* geo,
+                  const void* strided_workspace, size_t workspace_bytes,
+                  int32_t* gather_map, int64_t* meta, int64_t* status, void* stream);
+
 /* ---- strided kernel map --------------------------------------------------
  * Replaces generate_strided_indice_pairs (indices.py:143-259).  The output
  * set is found with an occupancy bitmap over the output grid (1 bit per

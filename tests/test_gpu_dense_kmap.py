@@ -72,3 +72,43 @@ def test_dense_out_of_grid_raises_and_leaves_table_clean(cuda):
     torch.cuda.synchronize()
     t = I._dense_table(cuda, L.stream_ptr(cuda), 1)
     assert int((t != -1).sum()) == 0
+
+
+def test_ranked_subm_map_on_strided_outputs_matches_table_maps(cuda):
+    """A SubM map on the output coordinates of a strided map reads its rows
+    from that map's occupancy bitmap (tsc_subm_kmap_ranked); it must equal
+    the direct-address and hash maps bit for bit, and an in-place change of
+    the coordinates must send the build back to a table."""
+    from trispconv_b200.pytorch.indices import generate_strided_indice_pairs
+
+    rng = np.random.default_rng(41)
+    shape = (12, 64, 64)
+    idx = torch.from_numpy(_cloud(rng, shape, 20000)).to(cuda)
+    for st, pd in ((2, 1), (1, 0)):
+        down = generate_strided_indice_pairs(idx, shape, 2, 3, st, pd)
+        out = down.out_indices
+        assert hasattr(out, "_tsc_ranked")
+        oshape = tuple(down.output_spatial_shape)
+        for ks, dl in ((3, 1), (3, 2), ((1, 3, 3), 1)):
+            a = I.generate_subm_indice_pairs(out, oshape, 2, ks, dl)
+            prev = I.RANKED
+            I.RANKED = False
+            try:
+                b = I.generate_subm_indice_pairs(out, oshape, 2, ks, dl)
+                prev_cells = I.DENSE_MAX_CELLS
+                I.DENSE_MAX_CELLS = 0  # the hash
+                try:
+                    c = I.generate_subm_indice_pairs(out, oshape, 2, ks, dl)
+                finally:
+                    I.DENSE_MAX_CELLS = prev_cells
+            finally:
+                I.RANKED = prev
+            torch.cuda.synchronize()
+            L.check_device_status(cuda)
+            for other in (b, c):
+                assert torch.equal(a._kmap.gather, other._kmap.gather), (st, ks, dl)
+                assert torch.equal(a._kmap.meta[L.META_COUNTS:], other._kmap.meta[L.META_COUNTS:])
+    # an in-place edit bumps the tensor's version: the rank table no longer applies
+    out2 = generate_strided_indice_pairs(idx, shape, 2, 3, 2, 1).out_indices
+    out2[:, 3].clamp_(max=100)  # no-op values, but a write
+    assert out2._tsc_ranked[3] != out2._version

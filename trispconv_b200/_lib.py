@@ -118,6 +118,7 @@ _SIGNATURES = {
     "tsc_subm_kmap": (ctypes.c_int, [_P, c_int64, POINTER(Geometry), _P, c_size_t, _P, _P, _P, _P]),
     "tsc_strided_kmap_workspace": (c_size_t, [POINTER(Geometry)]),
     "tsc_subm_kmap_dense": (ctypes.c_int, [_P, c_int64, POINTER(Geometry), _P, c_int64, _P, _P, _P, _P]),
+    "tsc_subm_kmap_ranked": (ctypes.c_int, [_P, c_int64, POINTER(Geometry), _P, c_size_t, _P, _P, _P, _P]),
     "tsc_strided_kmap_count": (ctypes.c_int, [_P, c_int64, POINTER(Geometry), _P, c_size_t, _P, _P, _P]),
     "tsc_strided_kmap_count_host": (ctypes.c_int, [_P, c_int64, POINTER(Geometry), _P, c_size_t, _P, _P, _P,
                                                    _P]),

@@ -18,6 +18,10 @@ namespace tsc {
 namespace detail {
 
 static_assert(tcp::KMAX == kPersistentKMax, "persistent kernel K limit");
+
+// The general store epilogue is needed for a folded BatchNorm or an
+// activation other than ReLU.
+inline bool epi_general(const EpiParams& e) { return e.scale != nullptr || e.act > TSC_ACT_RELU; }
 static_assert(mma::KMAX == kMmaKMax && tc::KMAX == kMmaKMax, "kernel K limits");
 
 // ---- tensor-core (mma.sync) path -------------------------------------------
@@ -210,16 +214,17 @@ int launch_tcp_cfg(const T* f, int64_t n_in, int c_in, const T* w, const T* bias
                    const int64_t* meta, T* out, int flags, const EpiParams& epi, int64_t* status, uint32_t* tile_counter,
                    cudaStream_t stream) {
   using C = tcp::Cfg<TN, KC>;
-  auto kern = tcp::k_conv_tcp<T, TN, KC>;
+  auto kern = epi_general(epi) ? tcp::k_conv_tcp<T, TN, KC, true> : tcp::k_conv_tcp<T, TN, KC, false>;
   CUtensorMap mf, mw;
   int rc = encode_maps<T, TN, KC>(f, n_in, c_in, w, K, c_out, &mf, &mw);
   if (rc != TSC_OK) return rc;
-  static unsigned long long configured = 0;
+  static unsigned long long configured[2] = {0, 0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
+  const int gen = epi_general(epi) ? 1 : 0;
+  if (!(configured[gen] & (1ull << (dev & 63)))) {
     TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL));
-    configured |= 1ull << (dev & 63);
+    configured[gen] |= 1ull << (dev & 63);
   }
   const int64_t tiles = ceil_div(n_out, tcp::BMT) * ceil_div(c_out, TN);
   const int64_t grid = tiles < sm_count() ? tiles : sm_count();
@@ -272,19 +277,20 @@ int launch_tcp(const void* F, int64_t n_in, int c_in, const void* W, const void*
 template <typename T, int TN, int NS>
 int launch_tmh_tn(const ConvArgs& a) {
   using C = tmh::Cfg<TN, NS>;
-  auto kern = tmh::k_conv_tmh<T, TN, NS>;
+  auto kern = epi_general(a.epi) ? tmh::k_conv_tmh<T, TN, NS, true> : tmh::k_conv_tmh<T, TN, NS, false>;
   const T* f = static_cast<const T*>(a.features);
   const T* w = static_cast<const T*>(a.weight);
   CUtensorMap mf, mw;
   // gather4 rows of 64 channels (the whole row) and weight boxes {64, 1, TN}
   int rc = encode_maps<T, TN, tmh::KC>(f, a.n_in, a.c_in, w, a.k_vol, a.c_out, &mf, &mw);
   if (rc != TSC_OK) return rc;
-  static unsigned long long configured = 0;
+  static unsigned long long configured[2] = {0, 0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(configured & (1ull << (dev & 63)))) {
+  const int gen = epi_general(a.epi) ? 1 : 0;
+  if (!(configured[gen] & (1ull << (dev & 63)))) {
     TSC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL));
-    configured |= 1ull << (dev & 63);
+    configured[gen] |= 1ull << (dev & 63);
   }
   const int64_t tiles = ceil_div(a.n_out, tmh::BMT);
   const int64_t grid = tiles < sm_count() ? tiles : sm_count();

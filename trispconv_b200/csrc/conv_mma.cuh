@@ -317,10 +317,7 @@ k_conv_mma(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict_
       uint4 v;
       T h[8];
     } pk;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      pk.h[i] = from_f32<T>(epi_apply(src[i], n + i, epi, bias));
-    }
+    epi_store8(src, n, epi, bias, pk.h);
     *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o) * c_out + n) = pk.v;
   }
 }
@@ -561,10 +558,7 @@ k_conv_mmaw(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict
         uint4 v;
         T h[8];
       } pk;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        pk.h[i] = from_f32<T>(epi_apply(src[i], n + i, epi, bias));
-      }
+      epi_store8(src, n, epi, bias, pk.h);
       *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o) * c_out + n) = pk.v;
     }
     __syncthreads();  // s_out, s_orow and s_rows are rewritten by the next tile

@@ -123,7 +123,10 @@ struct Cfg {
   static constexpr int SBO = 8 * KC * 2;
 };
 
-template <typename T, int TN, int KC>
+// GEN: the general store epilogue (folded BatchNorm scale/shift, any
+// activation); without it the store adds the bias and applies an optional
+// ReLU, the common case, in the shortest code.
+template <typename T, int TN, int KC, bool GEN>
 __global__ void __launch_bounds__(NT, 1)
 k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ CUtensorMap tmap_w,
            const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__ W,
@@ -343,6 +346,7 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
     // one column tile: the additive term of the store (bias, or the
     // epilogue's shift) is the same for every tile -> shared memory
     const bool bias_smem = n_col_tiles == 1;
+    const bool relu = epi.act == TSC_ACT_RELU;
     if (bias_smem) {
       for (int i = tid - EPI0; i < TN; i += NEPI)
         s_bias[i] = i >= c_out                ? 0.f
@@ -498,12 +502,20 @@ k_conv_tcp(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               float x = v[qq * 8 + i];
-              if (!bias_smem)
-                x = epi_apply(x, n + i, epi, bias);
-              else
-                x = activate(epi.scale != nullptr ? fmaf(x, __ldg(&epi.scale[n + i]), s_bias[n + i])
-                                                  : x + s_bias[n + i],
-                             epi.act, epi.alpha);
+              if constexpr (GEN) {
+                if (!bias_smem)
+                  x = epi_apply(x, n + i, epi, bias);
+                else
+                  x = activate(epi.scale != nullptr ? fmaf(x, __ldg(&epi.scale[n + i]), s_bias[n + i])
+                                                    : x + s_bias[n + i],
+                               epi.act, epi.alpha);
+              } else {
+                if (bias_smem)
+                  x += s_bias[n + i];
+                else if (bias != nullptr)
+                  x += to_f32(__ldg(&bias[n + i]));
+                if (relu) x = fmaxf(x, 0.f);
+              }
               pk.hv[i] = from_f32<T>(x);
             }
             *reinterpret_cast<uint4*>(out + static_cast<int64_t>(o) * c_out + n) = pk.u;

@@ -152,7 +152,9 @@ __device__ __forceinline__ HaloQuad load_halo_quad(const int32_t* __restrict__ h
   return h;
 }
 
-template <typename T, int TN, int NS_>
+// GEN: the general store epilogue (folded BatchNorm, any activation);
+// without it bias + optional ReLU in the shortest code.
+template <typename T, int TN, int NS_, bool GEN>
 __global__ void __launch_bounds__(NT, 1)
 k_conv_tmh(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ CUtensorMap tmap_w,
            const T* __restrict__ F, int64_t n_in, const T* __restrict__ bias, const int32_t* __restrict__ gmap,
@@ -332,9 +334,16 @@ k_conv_tmh(const __grid_constant__ CUtensorMap tmap_f, const __grid_constant__ C
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               const int n = c0 + qq * 8 + i;
-              const float x = epi.scale != nullptr ? fmaf(v[qq * 8 + i], __ldg(&epi.scale[n]), s_bias[n])
-                                                   : v[qq * 8 + i] + s_bias[n];
-              pk.hv[i] = from_f32<T>(activate(x, epi.act, epi.alpha));
+              float x;
+              if constexpr (GEN) {
+                x = activate(epi.scale != nullptr ? fmaf(v[qq * 8 + i], __ldg(&epi.scale[n]), s_bias[n])
+                                                  : v[qq * 8 + i] + s_bias[n],
+                             epi.act, epi.alpha);
+              } else {
+                x = v[qq * 8 + i] + s_bias[n];
+                if (epi.act == TSC_ACT_RELU) x = fmaxf(x, 0.f);
+              }
+              pk.hv[i] = from_f32<T>(x);
             }
             *reinterpret_cast<uint4*>(out + o * TN + c0 + qq * 8) = pk.u;
           }

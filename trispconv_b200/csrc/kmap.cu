@@ -202,6 +202,24 @@ struct HashLookup64 {
   }
 };
 
+// The output set of a strided map as its own lookup: a cell's row is the
+// rank of its bit in the occupancy bitmap (the order the strided map emitted
+// its output coordinates in), -1 when the bit is clear.
+template <typename KeyT>
+struct RankLookup {
+  const uint32_t* bitmap;
+  const uint32_t* word_prefix;
+  unsigned D, H, W;
+  __device__ __forceinline__ int operator()(unsigned b, unsigned z, unsigned y, unsigned x) const {
+    const KeyT lin = cell_key_t<KeyT>(b, z, y, x, D, H, W);
+    const KeyT w = lin >> 5;
+    const uint32_t word = __ldg(&bitmap[w]);
+    const uint32_t bit = 1u << static_cast<unsigned>(lin & 31u);
+    if (!(word & bit)) return -1;
+    return static_cast<int>(__ldg(&word_prefix[w]) + __popc(word & (bit - 1u)));
+  }
+};
+
 struct DenseLookup {
   const int32_t* table;
   unsigned D, H, W;
@@ -999,6 +1017,44 @@ int tsc_subm_kmap_dense(const int32_t* indices, int64_t n, const tsc_geometry* g
   TSC_LAUNCH_PDL("k_dense_clear", k_dense_clear, dim3(grid), dim3(kThreads), 0, stream, idx, n, g.B, g.D, g.H, g.W,
                  table);
   return TSC_OK;
+}
+
+int tsc_subm_kmap_ranked(const int32_t* indices, int64_t n, const tsc_geometry* geo, const void* strided_workspace,
+                         size_t workspace_bytes, int32_t* gather_map, int64_t* meta, int64_t* status, void* stream_) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int rc = check_geometry(geo, false);
+  if (rc != TSC_OK) return rc;
+  TSC_CHECK_ARG(n >= 0 && n <= 0x7fffffffLL, "number of voxels %lld out of range", (long long)n);
+  TSC_CHECK_ARG(meta != nullptr && status != nullptr, "meta/status must not be NULL");
+  const uint64_t cells = cells_of(geo->batch, geo->in_shape);
+  if (cells > kMaxCells64) {
+    set_error("grid batch*D*H*W = %llu exceeds the 64-bit key limit 2^62", (unsigned long long)cells);
+    return TSC_ERR_GRID_TOO_LARGE;
+  }
+  // the strided map's workspace over its output grid == this grid
+  tsc_geometry og = *geo;
+  for (int d = 0; d < 3; ++d) og.out_shape[d] = geo->in_shape[d];
+  const StridedWs w = strided_ws(og);
+  if (strided_workspace == nullptr || workspace_bytes < w.bytes || !aligned(strided_workspace, 256)) {
+    set_error("the strided workspace of this grid has %zu bytes (256-byte aligned), got %zu", w.bytes,
+              workspace_bytes);
+    return TSC_ERR_WORKSPACE;
+  }
+  const int K = geo->ksize[0] * geo->ksize[1] * geo->ksize[2];
+  rc = fill_words(meta, 0u, 2 * static_cast<int64_t>(TSC_META_COUNTS + K), nullptr, 0u, 0, stream);
+  if (rc != TSC_OK || n == 0) return rc;
+  TSC_CHECK_ARG(indices != nullptr && aligned(indices, 16), "indices must be 16-byte aligned");
+  TSC_CHECK_ARG(gather_map != nullptr && aligned(gather_map, 4), "gather_map must not be NULL");
+  const char* ws = static_cast<const char*>(strided_workspace);
+  const auto* bitmap = reinterpret_cast<const uint32_t*>(ws);
+  const auto* prefix = reinterpret_cast<const uint32_t*>(ws + w.off_prefix);
+  const GeoDev g = to_dev(*geo);
+  const int4* idx = reinterpret_cast<const int4*>(indices);
+  const unsigned D = static_cast<unsigned>(g.D), H = static_cast<unsigned>(g.H), W = static_cast<unsigned>(g.W);
+  if (cells > kMaxCells)
+    return launch_subm_query(idx, n, g, RankLookup<unsigned long long>{bitmap, prefix, D, H, W}, gather_map, meta,
+                             stream);
+  return launch_subm_query(idx, n, g, RankLookup<uint32_t>{bitmap, prefix, D, H, W}, gather_map, meta, stream);
 }
 
 size_t tsc_strided_kmap_workspace(const tsc_geometry* geo) {

@@ -159,7 +159,9 @@ __device__ __forceinline__ float activate(float x, int act, float alpha) {
   switch (act) {
     case TSC_ACT_RELU: return fmaxf(x, 0.f);
     case TSC_ACT_LEAKY_RELU: return x >= 0.f ? x : x * alpha;
-    case TSC_ACT_SILU: return x / (1.f + expf(-x));
+    // x * sigmoid(x) from the fast exponential and division intrinsics (a
+    // few ulp in fp32; -0 for very negative x)
+    case TSC_ACT_SILU: return __fdividef(x, 1.f + __expf(-x));
     default: return x;
   }
 }
@@ -171,6 +173,27 @@ __device__ __forceinline__ float epi_apply(float v, int n, const EpiParams& e, c
   else if (bias != nullptr)
     v += to_f32(bias[n]);
   return activate(v, e.act, e.alpha);
+}
+
+// Eight consecutive output channels n..n+7 of one row: the common bias (+
+// ReLU) store as its own loop, the general epilogue otherwise (one uniform
+// branch per eight values).
+template <typename T>
+__device__ __forceinline__ void epi_store8(const float* v, int n, const EpiParams& e, const T* __restrict__ bias,
+                                           T (&h)[8]) {
+  if (e.scale == nullptr && e.act <= TSC_ACT_RELU) {
+    const bool relu = e.act == TSC_ACT_RELU;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float x = v[i];
+      if (bias != nullptr) x += to_f32(bias[n + i]);
+      if (relu) x = fmaxf(x, 0.f);
+      h[i] = from_f32<T>(x);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = from_f32<T>(epi_apply(v[i], n + i, e, bias));
+  }
 }
 
 // Block-wide exclusive scan of one uint32 per thread (blockDim.x multiple of 32,

@@ -252,6 +252,9 @@ def _eager_check(device: torch.device) -> None:
 # dropping one returns its memory to that stream's cache after the work
 # queued there.
 DENSE_MAX_CELLS = int(os.environ.get("TRISPCONV_B200_DENSE_MAX_CELLS", str(1 << 28)))
+# SubM maps on the output coordinates of a strided map read their rows from
+# that map's occupancy bitmap (TRISPCONV_B200_RANKED=0: build a table instead).
+RANKED = os.environ.get("TRISPCONV_B200_RANKED", "1") != "0"
 DENSE_TABLES_PER_DEVICE = 2
 _dense_tables: "OrderedDict" = OrderedDict()
 
@@ -285,8 +288,18 @@ def generate_subm_indice_pairs(indices: torch.Tensor, spatial_shape, batch_size:
     meta = torch.empty(L.META_COUNTS + K, dtype=torch.int64, device=dev)
     cells = int(batch_size) * shape[0] * shape[1] * shape[2]
     stream = L.stream_ptr(dev)
+    ranked = getattr(indices, "_tsc_ranked", None)
+    if RANKED and ranked is not None and (ranked[1], ranked[2], ranked[3]) != (int(batch_size), shape,
+                                                                               indices._version):
+        ranked = None
     with L.on_device(dev):
-        if 0 < cells <= DENSE_MAX_CELLS:
+        if RANKED and ranked is not None:
+            ws = ranked[0]
+            ws.record_stream(torch.cuda.current_stream(dev))  # read on this stream too
+            L.check(lib.tsc_subm_kmap_ranked(idx.data_ptr(), n, L.byref(geo), ws.data_ptr(), ws.numel(),
+                                             gather.data_ptr(), meta.data_ptr(), L.status_word(dev).data_ptr(),
+                                             stream), "tsc_subm_kmap_ranked")
+        elif 0 < cells <= DENSE_MAX_CELLS:
             table = _dense_table(dev, stream, cells)
             L.check(lib.tsc_subm_kmap_dense(idx.data_ptr(), n, L.byref(geo), table.data_ptr(), table.numel(),
                                             gather.data_ptr(), meta.data_ptr(), L.status_word(dev).data_ptr(),
@@ -418,6 +431,10 @@ def finish_strided_indice_pairs(p) -> IndiceData:
                                           p.meta.data_ptr(), L.status_word(dev).data_ptr(), L.stream_ptr(dev)),
                 "tsc_strided_kmap_emit")
     _eager_check(dev)
+    # The workspace now holds the output grid's occupancy bitmap and its word
+    # prefix: a SubM map on these very coordinates looks its rows up there
+    # (tsc_subm_kmap_ranked) instead of building a table.
+    out_indices._tsc_ranked = (p.ws, int(p.batch_size), tuple(int(v) for v in p.out_shape), out_indices._version)
     km = KernelMap(K, n_in, n_out, gather, p.meta, dev, scatter=p.scatter, overflow=overflow,
                    overflow_cap=overflow.shape[0], pair_map=p.scatter, pair_mode=1, n_part=n_part)
     return IndiceData(out_indices=out_indices, pair_num=torch.tensor(counts, dtype=torch.long),
