@@ -130,12 +130,14 @@ def make_workload(args, rank: int, ws: int) -> BenchWorkload:
                              "weak", (0, wl.batch_size), ws * wl.n_voxels,
                              {"layers": 12, "box_voxels": wl.info.get("box_voxels")})
     c = args.channels
-    b0, b1 = shard.batch_range(16, rank, ws)
+    nb = getattr(args, "batch", 16)
+    b0, b1 = shard.batch_range(nb, rank, ws)
     idx = config5_coords(b0, b1)
     rng = np.random.default_rng(5)
     layers = syn.init_layers([syn.layer("subm", c, c, 3, key="subm")], rng, np.float16, bias_std=None)
-    return BenchWorkload(f"config5_subm3_c{c}_fp16", idx, None, (64, 512, 512), 16, layers, "strong", (b0, b1),
-                         16 * 500_000, {"layers": 1, "channels": c})
+    name = f"config5_subm3_c{c}_fp16" + ("" if nb == 16 else f"_batch{nb}")
+    return BenchWorkload(name, idx, None, (64, 512, 512), nb, layers, "strong", (b0, b1),
+                         nb * 500_000, {"layers": 1, "channels": c})
 
 
 # --------------------------------------------------------------------------
@@ -407,6 +409,12 @@ def conv_kernel_name(r: dict, flags: int, halo: bool = False) -> str:
             if halo and c_in == 64 and c_out in (64, 128) and k == 27 and r.get("no_overflow"):
                 return "k_conv_tmh"
             return "k_conv_tcp"
+        if (not flags & _lib.CONV_NO_RG and k <= 64 and
+                ((c_in in (4, 8) and c_out in (16, 32, 64)) or (c_in in (16, 32) and c_out in (16, 32)))):
+            # the register-gather kernel where its resident weights fit in
+            # 227 KB of shared memory (conv_rg.cu rg_smem_bytes)
+            if (k * c_in + 15) // 16 * (c_out // 16) * 512 <= 227 * 1024:
+                return "k_conv_rg"
         if k <= 64 and c_out % 8 == 0 and (c_in % 8 == 0 or (c_in % 4 == 0 and c_in <= 16)):
             return "k_conv_mma"
     return "k_conv_simt"
@@ -515,6 +523,16 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
+    # per-rank device time and host wall time of the timed steps (the
+    # straggler spread under torchrun)
+    mine = torch.tensor([local_ms / args.steps, wall * 1e3 / args.steps], dtype=torch.float64, device=dev)
+    every = [torch.zeros_like(mine) for _ in range(ws)]
+    if ws > 1:
+        dist.all_gather(every, mine)
+    else:
+        every = [mine]
+    per_rank = {"device_ms_per_step": [round(float(v[0]), 4) for v in every],
+                "host_wall_ms_per_step": [round(float(v[1]), 4) for v in every]}
     # voxels of one step over all ranks (each rank's own count, summed)
     nv = torch.tensor([wl.n_voxels], dtype=torch.float64, device=dev)
     if ws > 1:
@@ -717,6 +735,7 @@ def run_ours(args) -> None:
             "gather": gather,
             "clocks": clk,
             "wall_s_timed_region": wall,
+            "ranks": per_rank,
             "step_ms": [round(v, 4) for v in step_ms],
             "layers": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in r.items()} for r in step_rows],
         }
@@ -737,6 +756,8 @@ def main():
                          "config5: SubMConv3d C->C on one batch of 16 x 500k voxels split over the GPUs "
                          "(strong scaling)")
     ap.add_argument("--channels", type=int, default=256, choices=[64, 128, 256], help="config5 channels")
+    ap.add_argument("--batch", type=int, default=16,
+                    help="config5 batch (16, the benchmark's; smaller batches are for profiler captures)")
     ap.add_argument("--clock-log", default=None, help="file that receives the raw nvidia-smi clock samples")
     args = ap.parse_args()
     if args.warmup < 3:

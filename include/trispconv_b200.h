@@ -71,6 +71,8 @@ extern "C" {
 #define TSC_CONV_USE_TC     0x200  /* use the tcgen05 (TMEM) kernel where it applies */
 #define TSC_CONV_TC_SIMPLE  0x400  /* testing: one-tile-per-CTA tcgen05 kernel instead of the persistent one */
 #define TSC_CONV_NO_RESIDENT_W 0x800  /* testing: mma.sync kernel without resident weights */
+#define TSC_CONV_NO_RG      0x2000 /* testing: skip the register-gather kernel (C_in <= 32 layers then run
+                                      on the shared-memory mma.sync kernel) */
 #define TSC_CONV_TEST_WAIT_TIMEOUT 0x1000  /* testing: the persistent tcgen05 kernel computes nothing; one
                                               thread waits on a barrier nothing arrives at with a ~0.1 ms
                                               limit, which runs out and sets TSC_STATUS_WAIT_TIMEOUT (the

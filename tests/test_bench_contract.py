@@ -49,8 +49,14 @@ def test_reference_arm_prints_one_contract_line():
     (64, 128, 27, 2, _lib.CONV_USE_TC, True, "k_conv_tmh"),
     (64, 96, 27, 2, _lib.CONV_USE_TC, True, "k_conv_tcp"),
     (128, 128, 27, 2, _lib.CONV_USE_TC, True, "k_conv_tcp"),
-    (32, 32, 27, 2, _lib.CONV_USE_TC, False, "k_conv_mma"),
-    (4, 16, 27, 2, _lib.CONV_USE_TC, False, "k_conv_mma"),
+    (32, 32, 27, 2, _lib.CONV_USE_TC, False, "k_conv_rg"),
+    (4, 16, 27, 2, _lib.CONV_USE_TC, False, "k_conv_rg"),
+    (32, 64, 27, 2, _lib.CONV_USE_TC, False, "k_conv_mma"),
+    (8, 64, 27, 2, _lib.CONV_USE_TC, False, "k_conv_rg"),
+    (32, 32, 64, 2, _lib.CONV_USE_TC, False, "k_conv_rg"),
+    (32, 32, 27, 2, _lib.CONV_USE_TC | _lib.CONV_NO_RG, False, "k_conv_mma"),
+    (12, 16, 27, 2, _lib.CONV_USE_TC, False, "k_conv_mma"),
+    (32, 48, 27, 2, _lib.CONV_USE_TC, False, "k_conv_mma"),
     (64, 64, 27, 2, 0, False, "k_conv_mma"),
     (64, 64, 27, 4, _lib.CONV_USE_TC, False, "k_conv_simt"),
     (64, 64, 27, 2, _lib.CONV_USE_TC | _lib.CONV_FORCE_SIMT, False, "k_conv_simt"),

@@ -327,7 +327,7 @@ def test_mma_resident_weights_match_streamed_weights(cuda, cin, cout):
     w = (torch.randn(cout, 3, 3, 3, cin, device=cuda) * 0.1).half()
     b = torch.randn(cout, device=cuda).half()
     outs = []
-    for extra in (0, L.CONV_NO_RESIDENT_W):
+    for extra in (L.CONV_NO_RG, L.CONV_NO_RG | L.CONV_NO_RESIDENT_W):
         out = torch.empty(n, cout, dtype=torch.half, device=cuda)
         rc = L.load().tsc_conv_forward(f.data_ptr(), L.DTYPE_CODE[torch.float16], n, cin, w.data_ptr(), L.W_KRSC,
                                        b.data_ptr(), km.gather.data_ptr(), None, 27, n, cout, None, 0,

@@ -121,8 +121,10 @@ def test_fp32_cuda_core_epilogue(cuda, kind, act):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
 @pytest.mark.parametrize("cin,cout,kind,halo,simple", [
-    (16, 32, "subm", False, False),     # mma.sync
-    (32, 32, "spconv", False, False),   # mma.sync, strided (overflow-capable map)
+    (16, 32, "subm", False, False),     # register-gather mma.sync
+    (32, 32, "spconv", False, False),   # register-gather, strided (overflow-capable map)
+    (4, 16, "spconv", False, False),    # register-gather, 4 input channels
+    (8, 24, "subm", False, False),      # shared-memory mma.sync (C_out 24)
     (64, 64, "subm", False, False),     # persistent tcgen05 (TMA gather)
     (64, 128, "spconv", False, False),  # persistent tcgen05, strided
     (128, 96, "subm", False, False),    # persistent tcgen05, several column tiles

@@ -44,6 +44,7 @@ HALO_TILE_ROWS = 256  # output rows per tile of tsc_tile_halo
 HALO_PLANES = 3  # kz planes of a 3x3x3 kernel (the halo kernel's plane split)
 CONV_NO_RESIDENT_W = 0x800
 CONV_TEST_WAIT_TIMEOUT = 0x1000
+CONV_NO_RG = 0x2000
 
 W_KCC = 0   # (K, C_in, C_out)
 W_KRSC = 1  # (C_out, kD, kH, kW, C_in)

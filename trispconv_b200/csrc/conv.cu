@@ -270,6 +270,9 @@ int conv_forward(ConvArgs a, int32_t dtype, int32_t weight_layout) {
     if (n_in > 0 && tcp_eligible(dtype, w_krsc, c_in, c_out, k_vol) && (flags & TSC_CONV_TC_SIMPLE) == 0)
       return f16 ? launch_tcp_f16(a) : launch_tcp_bf16(a);
   }
+  if (!force_simt && (flags & TSC_CONV_NO_RG) == 0 && rg_eligible(dtype, w_krsc, c_in, c_out, k_vol) &&
+      n_out <= 0x7fffff00LL)
+    return f16 ? launch_rg_f16(a) : launch_rg_bf16(a);
   if (!force_simt && mma_eligible(dtype, w_krsc, c_in, c_out, k_vol))
     return f16 ? launch_mma_f16(a) : launch_mma_bf16(a);
   // the CUDA-core kernel walks rows in index order; results do not depend on

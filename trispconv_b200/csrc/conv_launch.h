@@ -85,6 +85,26 @@ inline bool tmh_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
 // channels (0 when it does not take c_out).
 int tmh_capacity(int c_out);
 
+// Register-gather kernel (conv_rg.cu): mma.sync with the A fragments loaded
+// straight from the gathered rows into registers and all weights resident in
+// shared memory.  16-bit types, KRSC weights, K <= 64 where the weights fit
+// in shared memory, C_in in {4, 8} with C_out in {16, 32, 64}, or C_in in
+// {16, 32} with C_out in {16, 32}.  Measured on the config-3 layers, the
+// shared-memory mma.sync kernel is faster for 32 -> 64 (131 against 144-300
+// us over the shapes tried), where the 110 KB of resident weights leave room
+// for too few warps per SM.
+size_t rg_smem_bytes(int c_in, int c_out, int K);
+bool rg_fits(int c_in, int c_out, int K);
+inline bool rg_eligible(int dtype, int w_krsc, int c_in, int c_out, int K) {
+  if (dtype != TSC_F16 && dtype != TSC_BF16) return false;
+  if (!w_krsc || K < 1 || K > 64) return false;
+  if (c_in != 4 && c_in != 8 && c_in != 16 && c_in != 32) return false;
+  if (c_out != 16 && c_out != 32 && (c_out != 64 || c_in > 8)) return false;
+  return rg_fits(c_in, c_out, K);
+}
+
+int launch_rg_f16(const ConvArgs& a);
+int launch_rg_bf16(const ConvArgs& a);
 int launch_mma_f16(const ConvArgs& a);
 int launch_mma_bf16(const ConvArgs& a);
 int launch_tc_f16(const ConvArgs& a);
