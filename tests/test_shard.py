@@ -88,3 +88,39 @@ def test_shard_gather_round_trip_two_gloo_ranks(batch, per):
     for _, gi, gf in results:
         np.testing.assert_array_equal(gi, idx.numpy())
         np.testing.assert_array_equal(gf, want_f)
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 dies between steps, before the output gather; rank 0 must get an
+    error from its next collective (short process-group timeout), not hang."""
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()  # flush the message before the hard exit
+        os._exit(3)
+    try:
+        gather_sparse(torch.zeros((2, 4), dtype=torch.int32), torch.zeros((2, 3)))
+        q.put((rank, "returned"))
+    except Exception as e:  # the failure the test expects
+        q.put((rank, "raised " + type(e).__name__))
+
+
+def test_gather_raises_when_a_rank_has_left():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert results[1] == "left" and procs[1].exitcode == 3
+    assert results[0].startswith("raised"), results[0]
+    assert procs[0].exitcode == 0
