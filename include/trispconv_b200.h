@@ -356,8 +356,8 @@ TSC_API int tsc_to_dense(const void* features, int32_t dtype, const int32_t* ind
  * gather_map[k][o] >= 0), masks ascending, so that the rows of a conv tile
  * share their kernel offsets; writes a permutation of [0, n_out) to
  * row_order, to be passed to tsc_conv_forward.  Convolution results do not
- * depend on it.  1 <= K <= 32.  More than 16384 distinct masks leave the
- * identity order. */
+ * depend on it.  1 <= K <= 32.  More than 16384 distinct masks, or a mask
+ * that finds no table slot within 128 probes, leave the identity order. */
 TSC_API size_t tsc_row_order_workspace(int64_t n_out);
 TSC_API int tsc_row_order(const int32_t* gather_map, int32_t k_vol, int64_t n_out, void* workspace,
                   size_t workspace_bytes, int32_t* row_order, int64_t* status, void* stream);
