@@ -10,12 +10,13 @@
 // (tile, plane) once and builds the A operands of the plane's offsets from it.
 //
 // One CTA per (tile, plane), one thread per tile row:
-//   1. the smallest and largest input row the (tile, plane) reads;
+//   1. the smallest and largest input row the (tile, plane) reads (each
+//      thread keeps its row's entries of the plane in registers);
 //   2. when they lie within kWindow rows of each other (spatially ordered
 //      maps: the outputs of strided maps and the submanifold maps built on
-//      them span a few hundred rows per plane), one bit per row of that
-//      window in shared memory, set by every pair; a prefix popcount over
-//      the window ranks the distinct rows in ascending order.  The first
+//      them span a few hundred rows per plane), one bit per row of the span
+//      in shared memory, set by every pair; a prefix popcount over the
+//      span's words ranks the distinct rows in ascending order.  The first
 //      `capacity` ranks form the list, padded to a multiple of 4 with copies
 //      of its last row (TMA gathers 4 rows);
 //   3. every pair's entry becomes its rank, kOutsideHalo when the rank is
@@ -68,18 +69,25 @@ __global__ void __launch_bounds__(kThreads) k_tile_plane_halo(const int32_t* __r
     s_kmask = 0u;
   }
   __syncthreads();
+  // the plane's gather entries of this row, read once
+  int v[kMaxK];
   int lo = 0x7fffffff, hi = -1;
   unsigned km = 0u;
-  for (int j = 0; j < kpg; ++j) {
-    int v = row_ok ? __ldg(&gmap[static_cast<int64_t>(k0 + j) * n_out + o]) : -1;
-    if (v >= n_in) {
-      raise_status(status, TSC_STATUS_KEY_RANGE);
-      v = -1;
-    }
-    if (v >= 0) {
-      lo = min(lo, v);
-      hi = max(hi, v);
-      km |= 1u << (k0 + j);
+#pragma unroll
+  for (int j = 0; j < kMaxK; ++j) {
+    v[j] = -1;
+    if (j < kpg) {
+      int e = row_ok ? __ldg(&gmap[static_cast<int64_t>(k0 + j) * n_out + o]) : -1;
+      if (e >= n_in) {
+        raise_status(status, TSC_STATUS_KEY_RANGE);
+        e = -1;
+      }
+      if (e >= 0) {
+        lo = min(lo, e);
+        hi = max(hi, e);
+        km |= 1u << (k0 + j);
+      }
+      v[j] = e < 0 ? -1 : e;
     }
   }
   // warp-level reduction first, then one shared atomic per warp
@@ -94,7 +102,6 @@ __global__ void __launch_bounds__(kThreads) k_tile_plane_halo(const int32_t* __r
     atomicMax(&s_hi, hi);
     atomicOr(&s_kmask, km);
   }
-  for (int i = tid; i < kWindowWords; i += kThreads) bits[i] = 0u;
   __syncthreads();
   const int base = s_lo;
   const bool any = s_hi >= 0;
@@ -107,32 +114,37 @@ __global__ void __launch_bounds__(kThreads) k_tile_plane_halo(const int32_t* __r
     // every pair reads its row from global memory
     if (tid == 0) halo_count[hp] = 0;
     if (!row_ok) return;
-    for (int j = 0; j < kpg; ++j) {
-      const int v = __ldg(&gmap[static_cast<int64_t>(k0 + j) * n_out + o]);
-      hmap[static_cast<int64_t>(k0 + j) * n_out + o] =
-          static_cast<int16_t>(v >= 0 && v < n_in ? kOutsideHalo : kNoPair);
-    }
+#pragma unroll
+    for (int j = 0; j < kMaxK; ++j)
+      if (j < kpg)
+        hmap[static_cast<int64_t>(k0 + j) * n_out + o] = static_cast<int16_t>(v[j] >= 0 ? kOutsideHalo : kNoPair);
     return;
   }
 
-  for (int j = 0; j < kpg; ++j) {
-    const int v = row_ok ? __ldg(&gmap[static_cast<int64_t>(k0 + j) * n_out + o]) : -1;
-    if (v >= 0 && v < n_in) {
-      const int b = v - base;
+  // only the words the rows span: [base, s_hi]
+  const int nwords = ((s_hi - base) >> 5) + 1;  // 1 .. kWindowWords
+  for (int i = tid; i < nwords; i += kThreads) bits[i] = 0u;
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kMaxK; ++j) {
+    if (j < kpg && v[j] >= 0) {
+      const int b = v[j] - base;
       atomicOr(&bits[b >> 5], 1u << (b & 31));
     }
   }
   __syncthreads();
-  // ranks: exclusive prefix of the popcounts, thread tid owning words
-  // tid*8 .. tid*8+7
+  // ranks: exclusive prefix of the popcounts; thread tid owns words
+  // tid*wpt .. tid*wpt+wpt-1 of the span
+  const int wpt = (nwords + kThreads - 1) / kThreads;  // 1 .. kWordsPerThread
+  const int w0 = tid * wpt;
   uint32_t cnt = 0;
-#pragma unroll
-  for (int i = 0; i < kWordsPerThread; ++i) cnt += __popc(bits[tid * kWordsPerThread + i]);
+  for (int i = 0; i < wpt; ++i)
+    if (w0 + i < nwords) cnt += __popc(bits[w0 + i]);
   uint32_t total = 0;
   uint32_t run = block_exclusive_scan(cnt, warp_sums, &total);
-#pragma unroll
-  for (int i = 0; i < kWordsPerThread; ++i) {
-    const int w = tid * kWordsPerThread + i;
+  for (int i = 0; i < wpt; ++i) {
+    const int w = w0 + i;
+    if (w >= nwords) break;
     word_pre[w] = run;
     uint32_t m = bits[w];
     while (m) {
@@ -153,7 +165,7 @@ __global__ void __launch_bounds__(kThreads) k_tile_plane_halo(const int32_t* __r
     if (i < ((hc + 3) & ~3)) {
       // find the row of rank hc-1
       const uint32_t want = static_cast<uint32_t>(hc - 1);
-      int lo_w = 0, hi_w = kWindowWords - 1;
+      int lo_w = 0, hi_w = nwords - 1;
       while (lo_w < hi_w) {  // last word whose prefix is <= want
         const int mid = (lo_w + hi_w + 1) >> 1;
         if (word_pre[mid] <= want) lo_w = mid; else hi_w = mid - 1;
@@ -171,11 +183,12 @@ __global__ void __launch_bounds__(kThreads) k_tile_plane_halo(const int32_t* __r
     }
   }
   if (!row_ok) return;
-  for (int j = 0; j < kpg; ++j) {
-    const int v = __ldg(&gmap[static_cast<int64_t>(k0 + j) * n_out + o]);
+#pragma unroll
+  for (int j = 0; j < kMaxK; ++j) {
+    if (j >= kpg) break;
     int hv = kNoPair;
-    if (v >= 0 && v < n_in) {
-      const int b = v - base;
+    if (v[j] >= 0) {
+      const int b = v[j] - base;
       const uint32_t rank = word_pre[b >> 5] + __popc(bits[b >> 5] & ((1u << (b & 31)) - 1u));
       hv = rank < static_cast<uint32_t>(cap) ? static_cast<int>(rank) : kOutsideHalo;
     }
