@@ -124,6 +124,16 @@ def make_workload(args, rank: int, ws: int) -> BenchWorkload:
     from trispconv_b200 import shard
     from trispconv_b200.testing import synthetic as syn
 
+    if args.workload == "config3" and getattr(args, "scaling", "weak") == "strong":
+        # one batch of 4 split by sample over the ranks (global batch ids kept)
+        if ws > 4:
+            raise SystemExit("config3 strong scaling splits a batch of 4: at most 4 GPUs")
+        wl = syn.config3(seed=3, batch=4)
+        b0, b1 = shard.batch_range(4, rank, ws)
+        keep = (wl.indices[:, 0] >= b0) & (wl.indices[:, 0] < b1)
+        return BenchWorkload(WORKLOAD + "_strong", np.ascontiguousarray(wl.indices[keep]),
+                             np.ascontiguousarray(wl.features[keep]), wl.spatial_shape, wl.batch_size, wl.layers,
+                             "strong", (b0, b1), wl.n_voxels, {"layers": 12, "box_voxels": wl.info.get("box_voxels")})
     if args.workload == "config3":
         wl = syn.config3(seed=3 + 1000 * rank, batch=4)
         return BenchWorkload(WORKLOAD, wl.indices, wl.features, wl.spatial_shape, wl.batch_size, wl.layers,
@@ -756,6 +766,9 @@ def main():
                          "config5: SubMConv3d C->C on one batch of 16 x 500k voxels split over the GPUs "
                          "(strong scaling)")
     ap.add_argument("--channels", type=int, default=256, choices=[64, 128, 256], help="config5 channels")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="config3: weak (a batch of 4 per GPU, the default) or strong (one batch of 4 split over "
+                         "up to 4 GPUs)")
     ap.add_argument("--batch", type=int, default=16,
                     help="config5 batch (16, the benchmark's; smaller batches are for profiler captures)")
     ap.add_argument("--clock-log", default=None, help="file that receives the raw nvidia-smi clock samples")

@@ -92,6 +92,29 @@ def test_weight_normalizer():
         normalize_spconv_weight(torch.randn(2, 2), (3, 3, 3), 4, 8)
 
 
+def test_krsc_checkpoint_tensors_load_and_normalize():
+    """KRSC checkpoint tensors of a decoder upsample block (the shapes of
+    the reference's checkpoint test, tests/test_anigen_weights.py, drawn at
+    random here) load into the modules by state_dict and normalise to
+    (K, C_in, C_out), the 1x1x1 inverse conv through the flat quirk."""
+    torch.manual_seed(3)
+    blocks = {
+        "inv3": (spconv.SparseInverseConv3d(768, 192, 3, indice_key="u0"), (192, 3, 3, 3, 768)),
+        "subm3": (spconv.SubMConv3d(192, 192, 3), (192, 3, 3, 3, 192)),
+        "inv1": (spconv.SparseInverseConv3d(768, 192, 1, indice_key="u1"), (192, 1, 1, 1, 768)),
+    }
+    for name, (m, shape) in blocks.items():
+        assert tuple(m.weight.shape) == shape, name
+        sd = {"weight": torch.randn(shape), "bias": torch.randn(192)}
+        m.load_state_dict(sd)
+        assert torch.equal(m.weight.data, sd["weight"]) and torch.equal(m.bias.data, sd["bias"])
+        K = shape[1] * shape[2] * shape[3]
+        n = normalize_spconv_weight(m.weight.data, shape[1:4], shape[4], shape[0])
+        assert n.shape == (K, shape[4], shape[0]), name
+    with pytest.raises(RuntimeError):  # a transposed (K, C_in, C_out) tensor is not a KRSC parameter
+        blocks["subm3"][0].load_state_dict({"weight": torch.randn(27, 192, 192), "bias": torch.randn(192)})
+
+
 def test_kernel_weight_views_match_normalizer():
     """The conv kernel reads the KRSC parameter in place; check that the
     layouts it is handed address exactly normalize_spconv_weight's values."""
