@@ -123,7 +123,9 @@ TSC_API unsigned long long tsc_launch_count(void);
  * `table[encoded] = arange` write order).  meta[TSC_META_COUNTS + k] receives
  * pair_num[k].  Keys are 32-bit up to batch*D*H*W = 2^32 - 2 cells and
  * 64-bit above (the reference's int64 key, indices.py:45-51), up to 2^62
- * cells; tsc_subm_kmap_workspace covers both. */
+ * cells; tsc_subm_kmap_workspace covers both.  The hash takes 2^ceil(log2 8n)
+ * slots when the workspace holds them (tsc_subm_kmap_workspace's size), and
+ * at least 2^ceil(log2 2n): a smaller workspace fails with TSC_ERR_WORKSPACE. */
 TSC_API size_t tsc_subm_kmap_workspace(int64_t n);
 TSC_API int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo,
                   void* workspace, size_t workspace_bytes,

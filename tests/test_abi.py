@@ -45,10 +45,11 @@ def test_abi_version_and_introspection(lib):
 
 
 def test_workspace_sizes(lib):
-    # 12 bytes per slot (a 64-bit key + a row, for grids above 2^32 - 2 cells)
-    assert lib.tsc_subm_kmap_workspace(0) == 12 << 8
-    assert lib.tsc_subm_kmap_workspace(1000) == 12 << 11         # 2n rounded up to 2^11
-    assert lib.tsc_subm_kmap_workspace(160000) == 12 << 19
+    # 12 bytes per slot (a 64-bit key + a row, for grids above 2^32 - 2 cells),
+    # 2^ceil(log2 8n) slots (at least 2^10)
+    assert lib.tsc_subm_kmap_workspace(0) == 12 << 10
+    assert lib.tsc_subm_kmap_workspace(1000) == 12 << 13         # 8n rounded up to 2^13
+    assert lib.tsc_subm_kmap_workspace(160000) == 12 << 21
     g = L.make_geometry(4, (41, 1600, 1408), (21, 800, 704), (3, 3, 3), (2, 2, 2), (1, 1, 1))
     ws = lib.tsc_strided_kmap_workspace(ctypes.byref(g))
     bits = 4 * 21 * 800 * 704
@@ -79,8 +80,9 @@ def test_host_side_argument_checks(lib):
     wide = L.make_geometry(1 << 20, (1 << 10, 1 << 10, 1 << 10), (1 << 10, 1 << 10, 1 << 10), (3, 3, 3))
     rc = lib.tsc_subm_kmap(1 << 20, 1, ctypes.byref(wide), 1 << 20, 16, 1 << 20, ctypes.addressof(m),
                            ctypes.addressof(s), None)
-    assert rc == L.TSC_ERR_WORKSPACE and str(lib.tsc_subm_kmap_workspace(1)) in L.last_error()
-    assert lib.tsc_subm_kmap_workspace(1) == 12 << 8
+    # the message names the smallest workspace the call takes: 12 bytes x 2^8 slots
+    assert rc == L.TSC_ERR_WORKSPACE and str(12 << 8) in L.last_error()
+    assert lib.tsc_subm_kmap_workspace(1) == 12 << 10
     rc = lib.tsc_conv_forward(None, 0, 10, 0, None, 0, None, None, None, 27, 10, 8, None, 0, None, None, 0,
                               ctypes.addressof(s), None, None)
     assert rc == L.TSC_ERR_INVALID_ARG

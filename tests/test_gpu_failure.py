@@ -10,8 +10,8 @@
   on those SMs wait).
 * Host-side refusals through the C ABI: an undersized hash workspace
   (TSC_ERR_WORKSPACE).  TSC_STATUS_HASH_FULL itself cannot be reached through
-  the ABI: the caller's workspace must hold 2^ceil(log2 2n) slots (load
-  factor <= 1/2) and the probe loop may visit every slot.
+  the ABI: the caller's workspace must hold at least 2^ceil(log2 2n) slots
+  (load factor <= 1/2) and the probe loop may visit every slot.
 * A device-side range error: a coordinate outside the grid sets
   TSC_STATUS_KEY_RANGE, which the Python layer raises as RuntimeError.
 """
@@ -81,8 +81,8 @@ def test_subm_kmap_refuses_an_undersized_workspace(cuda):
     n = 5000
     idx = torch.from_numpy(_cloud(rng, (30, 30, 30), n)).to(cuda)
     geo = L.make_geometry(1, (30, 30, 30), (30, 30, 30), (3, 3, 3))
-    need = int(lib.tsc_subm_kmap_workspace(n))
-    ws = torch.empty(need // 2, dtype=torch.uint8, device=cuda)
+    need = int(lib.tsc_subm_kmap_workspace(n))  # 12 bytes x 2^ceil(log2 8n) slots
+    ws = torch.empty(need // 8, dtype=torch.uint8, device=cuda)  # below 8 bytes x 2^ceil(log2 2n)
     gather = torch.empty((27, n), dtype=torch.int32, device=cuda)
     meta = torch.empty(L.META_COUNTS + 27, dtype=torch.int64, device=cuda)
     status = torch.zeros(1, dtype=torch.int64, device=cuda)

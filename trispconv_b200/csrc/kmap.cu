@@ -54,9 +54,22 @@ int log2_ceil(uint64_t v) {
 }
 
 // Capacity of the submanifold hash: load factor <= 1/2.
+// Smallest SubM hash: 2^ceil(log2 2n) slots (load factor <= 1/2).
 int subm_log2cap(int64_t n) {
   int l = log2_ceil(static_cast<uint64_t>(n < 1 ? 1 : n) * 2);
   return l < 8 ? 8 : l;
+}
+
+// The workspace entry point takes up to 4x that (load factor <= 1/8) when the
+// caller's workspace holds it: on the config-3 input map a lookup that misses
+// then walks 1.14 slots on average instead of 2.03 (1.10 instead of 1.55 for a
+// hit), one dependent L2 round trip each.
+constexpr int kSubmSpread = 2;
+int subm_ws_log2cap(int64_t n, size_t workspace_bytes, size_t slot_bytes) {
+  const int lo = subm_log2cap(n);
+  for (int l = lo + kSubmSpread; l > lo; --l)
+    if ((slot_bytes << l) <= workspace_bytes) return l;
+  return lo;
 }
 
 __device__ __forceinline__ bool in_grid(const int4& c, int B, int D, int H, int W) {
@@ -417,12 +430,11 @@ k_strided_mark(const int4* __restrict__ idx, int64_t n, GeoDev g, uint32_t* __re
         const bool v = active && vy && exact_div(c.w + g.px - kx * g.dx, g.sx, g.oW, ox);
         const unsigned b = __ballot_sync(kFullMask, v);
         if (v) {
-          // Lanes that hit the same bitmap word combine their bits; one atomic per word.
+          // one fire-and-forget OR per candidate: combining the lanes of a
+          // word first (__match_any_sync) saved only ~10 % of the atomics on
+          // the config-3 maps and cost more instructions than it saved
           const KeyT lin = cell_key_t<KeyT>(c.x, oz, oy, ox, g.oD, g.oH, g.oW);
-          const KeyT word = lin >> 5;
-          const unsigned same = __match_any_sync(b, word);
-          const unsigned bits = __reduce_or_sync(same, 1u << static_cast<unsigned>(lin & 31u));
-          if (lane == __ffs(same) - 1) atomicOr(&bitmap[word], bits);
+          atomicOr(&bitmap[lin >> 5], 1u << static_cast<unsigned>(lin & 31u));
           any = true;
         }
         if (lane == 0 && b) atomicAdd(&s_cnt[k], static_cast<unsigned>(__popc(b)));
@@ -928,7 +940,7 @@ extern "C" {
 size_t tsc_subm_kmap_workspace(int64_t n) {
   // 8-byte key|row slots for grids of at most 2^32-2 cells; above, 8-byte
   // keys plus 4-byte rows per slot (the larger of the two)
-  return static_cast<size_t>(12) << subm_log2cap(n);
+  return static_cast<size_t>(12) << (subm_log2cap(n) + kSubmSpread);
 }
 
 int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo, void* workspace,
@@ -950,12 +962,13 @@ int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo, vo
   if (n == 0) return fill_words(meta, 0u, meta_words, nullptr, 0u, 0, stream);
   TSC_CHECK_ARG(indices != nullptr && aligned(indices, 16), "indices must be 16-byte aligned");
   TSC_CHECK_ARG(gather_map != nullptr && aligned(gather_map, 4), "gather_map must not be NULL");
-  const int log2cap = subm_log2cap(n);
-  const size_t need = static_cast<size_t>(wide ? 12 : 8) << log2cap;
+  const size_t slot_bytes = wide ? 12 : 8;
+  const size_t need = slot_bytes << subm_log2cap(n);
   if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16)) {
     set_error("subm workspace needs %zu bytes (16-byte aligned), got %zu", need, workspace_bytes);
     return TSC_ERR_WORKSPACE;
   }
+  const int log2cap = subm_ws_log2cap(n, workspace_bytes, slot_bytes);
   if (wide) {
     // keys (all ones = empty) then rows (-1), one fill with meta = 0
     auto* keys = static_cast<unsigned long long*>(workspace);
@@ -974,7 +987,7 @@ int tsc_subm_kmap(const int32_t* indices, int64_t n, const tsc_geometry* geo, vo
   }
   auto* table = static_cast<unsigned long long*>(workspace);
   // meta = 0 and every table slot empty (all ones), one launch
-  rc = fill_words(meta, 0u, meta_words, table, 0xFFFFFFFFu, static_cast<int64_t>(need / 4), stream);
+  rc = fill_words(meta, 0u, meta_words, table, 0xFFFFFFFFu, static_cast<int64_t>(2) << log2cap, stream);
   if (rc != TSC_OK) return rc;
   const GeoDev g = to_dev(*geo);
   const int4* idx = reinterpret_cast<const int4*>(indices);
