@@ -595,6 +595,10 @@ def run_ours(args) -> None:
     roof["algorithmic_flops_per_launch"] = dom_flops / n_dom
     roof["ms_per_launch"] = dom_ms / n_dom
     roof["peak_source"] = peaks["source"]
+    # the same fraction at the maximum SM clock: the peaks were measured at it,
+    # and a run held below it by the power cap scales its compute-bound time
+    if clk and clk.get("sm_mhz") and clk.get("sm_max_mhz"):
+        roof["frac_clock_normalised"] = roof["frac"] * float(clk["sm_max_mhz"]) / float(clk["sm_mhz"])
     roof["share_of_conv_time"] = fam_ms[dom] / sum(fam_ms.values())
 
     # ---- e2e through the public API with host buffers --------------------
