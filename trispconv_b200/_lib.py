@@ -110,6 +110,24 @@ def make_geometry(batch, in_shape, out_shape, ksize, stride=(1, 1, 1), padding=(
     return g
 
 
+_GEOMETRIES: Dict[tuple, Geometry] = {}
+
+
+def geometry(batch, in_shape, out_shape, ksize, stride=(1, 1, 1), padding=(0, 0, 0),
+             dilation=(1, 1, 1)) -> Geometry:
+    """make_geometry for the hot path: one shared, read-only struct per
+    distinct geometry (the library copies it during the call).  Callers
+    must not modify the returned struct."""
+    key = (int(batch), tuple(in_shape), tuple(out_shape), tuple(ksize), tuple(stride), tuple(padding),
+           tuple(dilation))
+    g = _GEOMETRIES.get(key)
+    if g is None:
+        if len(_GEOMETRIES) > 4096:
+            _GEOMETRIES.clear()
+        g = _GEOMETRIES[key] = make_geometry(batch, in_shape, out_shape, ksize, stride, padding, dilation)
+    return g
+
+
 _P = c_void_p
 _SIGNATURES = {
     "tsc_abi_version": (ctypes.c_int, []),

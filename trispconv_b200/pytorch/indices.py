@@ -283,7 +283,7 @@ def generate_subm_indice_pairs(indices: torch.Tensor, spatial_shape, batch_size:
     n = idx.shape[0]
     K = ks[0] * ks[1] * ks[2]
     lib = L.load()
-    geo = L.make_geometry(batch_size, shape, shape, ks, (1, 1, 1), (0, 0, 0), dl)
+    geo = L.geometry(batch_size, shape, shape, ks, (1, 1, 1), (0, 0, 0), dl)
     gather = torch.empty((K, n), dtype=torch.int32, device=dev)
     meta = torch.empty(L.META_COUNTS + K, dtype=torch.int64, device=dev)
     cells = int(batch_size) * shape[0] * shape[1] * shape[2]
@@ -382,7 +382,7 @@ def start_strided_indice_pairs(indices: torch.Tensor, spatial_shape, batch_size:
     p = PendingStrided()
     p.indices, p.idx, p.spatial_shape, p.out_shape, p.batch_size = indices, idx, spatial_shape, out_shape, batch_size
     p.ks, p.st, p.pd, p.dl, p.K = ks, st, pd, dl, K
-    p.geo = L.make_geometry(batch_size, shape, out_shape, ks, st, pd, dl)
+    p.geo = L.geometry(batch_size, shape, out_shape, ks, st, pd, dl)
     p.ws = L.workspace(lib.tsc_strided_kmap_workspace(L.byref(p.geo)), dev)
     p.meta = torch.empty(L.META_COUNTS + K, dtype=torch.int64, device=dev)
     p.scatter = torch.empty((K, n_in), dtype=torch.int32, device=dev)  # size known before the count
