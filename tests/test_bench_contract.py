@@ -93,3 +93,27 @@ def test_clock_sampler_reads_median_clock_and_throttle_reasons(tmp_path):
 def test_clock_sampler_without_nvidia_smi():
     s = bench.ClockSampler(0)
     assert s.stop()["reasons"] == ["nvidia-smi unavailable"]
+
+
+def test_config3_strong_scaling_splits_one_batch_by_sample():
+    """--scaling strong: the ranks share one batch of 4, each with whole
+    samples, global batch ids and the global batch size; their rows together
+    are the batch's rows in order."""
+    import argparse
+
+    import numpy as np
+
+    args = argparse.Namespace(workload="config3", scaling="strong", channels=256, batch=16)
+    whole = bench.make_workload(args, 0, 1)
+    for ws in (2, 4):
+        parts = [bench.make_workload(args, r, ws) for r in range(ws)]
+        assert all(p.scaling == "strong" and p.batch_size == 4 for p in parts)
+        assert all(p.total_voxels == whole.n_voxels for p in parts)
+        assert [p.samples for p in parts] == [((4 * r) // ws, (4 * (r + 1)) // ws) for r in range(ws)]
+        for p in parts:
+            b = p.indices[:, 0]
+            assert b.min() >= p.samples[0] and b.max() < p.samples[1]
+        np.testing.assert_array_equal(np.concatenate([p.indices for p in parts]), whole.indices)
+        np.testing.assert_array_equal(np.concatenate([p.features for p in parts]), whole.features)
+    with pytest.raises(SystemExit):
+        bench.make_workload(args, 0, 8)
