@@ -27,13 +27,15 @@ def _ulp(dtype):
     return 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10
 
 
-def _raw(cuda, f, w, bias, gmap, k_vol, n_out, flags, ovf=None, meta=None):
-    """tsc_conv_forward on a hand-built k-major gather map (None = identity)."""
+def _raw(cuda, f, w, bias, gmap, k_vol, n_out, flags, ovf=None, meta=None, order=None):
+    """tsc_conv_forward on a hand-built k-major gather map (None = identity)
+    and optional row order."""
     cout = w.shape[0]
     out = torch.full((n_out, cout), float("nan"), dtype=f.dtype, device=cuda)
     rc = L.load().tsc_conv_forward(
         f.data_ptr() if f.numel() else None, L.DTYPE_CODE[f.dtype], f.shape[0], f.shape[1], w.data_ptr(), L.W_KRSC,
-        None if bias is None else bias.data_ptr(), None if gmap is None else gmap.data_ptr(), None, k_vol, n_out,
+        None if bias is None else bias.data_ptr(), None if gmap is None else gmap.data_ptr(),
+        None if order is None else order.data_ptr(), k_vol, n_out,
         cout, None if ovf is None else ovf.data_ptr(), 0 if ovf is None else ovf.shape[0],
         None if meta is None else meta.data_ptr(), out.data_ptr(), flags, L.status_word(cuda).data_ptr(), None,
         L.stream_ptr(cuda))
@@ -181,3 +183,28 @@ def test_row_order_gives_identical_bits(cuda, cin, cout):
     torch.cuda.synchronize()
     L.check_device_status(cuda)
     assert torch.equal(a.features, b.features)
+
+
+@pytest.mark.parametrize("cin,cout", [(16, 32), (8, 24)], ids=["register-gather", "shared-memory-mma"])
+def test_row_order_entry_out_of_range_is_reported(cuda, cin, cout):
+    """A row order that is not a permutation of the output rows (one entry
+    equal to n_out) sets TSC_STATUS_INTERNAL; that row is skipped and every
+    other row is still computed."""
+    rng = np.random.default_rng(cin + cout)
+    n = 700
+    f = torch.from_numpy(rng.standard_normal((n, cin)).astype(np.float32)).to(cuda).half()
+    w = (torch.randn(cout, 27, cin, device=cuda) * 0.1).half()
+    g = torch.from_numpy(_random_map(rng, 27, n, n, 0.3)).to(cuda)
+    ref = _raw(cuda, f, w, None, g, 27, n, 0)
+    torch.cuda.synchronize()
+    L.check_device_status(cuda)
+    order = torch.arange(n, dtype=torch.int32, device=cuda)
+    order[123] = n  # row 123 is never produced, and the entry is out of range
+    got = _raw(cuda, f, w, None, g, 27, n, 0, order=order)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="out-of-range index"):
+        L.check_device_status(cuda)
+    keep = torch.ones(n, dtype=torch.bool, device=cuda)
+    keep[123] = False
+    assert torch.equal(got[keep], ref[keep])
+    assert torch.isnan(got[123]).all()

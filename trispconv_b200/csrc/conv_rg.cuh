@@ -283,7 +283,12 @@ k_conv_rg(const T* __restrict__ F, int n_in, const T* __restrict__ W, const T* _
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int t = t0 + mt * 16 + h * 8 + grp;
-        o[mt][h] = t < n_out ? (perm != nullptr ? __ldg(&perm[t]) : t) : -1;
+        int ov = t < n_out ? (perm != nullptr ? __ldg(&perm[t]) : t) : -1;
+        if (t < n_out && static_cast<unsigned>(ov) >= static_cast<unsigned>(n_out)) {
+          raise_status(status, TSC_STATUS_INTERNAL);  // a row order that is not a permutation of the rows
+          ov = -1;
+        }
+        o[mt][h] = ov;
         mrow[mt][h] = o[mt][h] < 0 ? nullptr
                       : (ident ? gmap_self : gmap + static_cast<int64_t>(loff) * n_out + o[mt][h]);
       }
