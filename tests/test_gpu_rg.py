@@ -185,8 +185,10 @@ def test_row_order_gives_identical_bits(cuda, cin, cout):
     assert torch.equal(a.features, b.features)
 
 
-@pytest.mark.parametrize("cin,cout", [(16, 32), (8, 24)], ids=["register-gather", "shared-memory-mma"])
-def test_row_order_entry_out_of_range_is_reported(cuda, cin, cout):
+@pytest.mark.parametrize("cin,cout,flags", [(16, 32, 0), (8, 24, 0), (64, 64, L.CONV_USE_TC | L.CONV_TC_SIMPLE),
+                                            (64, 64, L.CONV_USE_TC)],
+                         ids=["register-gather", "shared-memory-mma", "tcgen05-one-tile", "tcgen05-persistent"])
+def test_row_order_entry_out_of_range_is_reported(cuda, cin, cout, flags):
     """A row order that is not a permutation of the output rows (one entry
     equal to n_out) sets TSC_STATUS_INTERNAL; that row is skipped and every
     other row is still computed."""
@@ -195,12 +197,12 @@ def test_row_order_entry_out_of_range_is_reported(cuda, cin, cout):
     f = torch.from_numpy(rng.standard_normal((n, cin)).astype(np.float32)).to(cuda).half()
     w = (torch.randn(cout, 27, cin, device=cuda) * 0.1).half()
     g = torch.from_numpy(_random_map(rng, 27, n, n, 0.3)).to(cuda)
-    ref = _raw(cuda, f, w, None, g, 27, n, 0)
+    ref = _raw(cuda, f, w, None, g, 27, n, flags)
     torch.cuda.synchronize()
     L.check_device_status(cuda)
     order = torch.arange(n, dtype=torch.int32, device=cuda)
     order[123] = n  # row 123 is never produced, and the entry is out of range
-    got = _raw(cuda, f, w, None, g, 27, n, 0, order=order)
+    got = _raw(cuda, f, w, None, g, 27, n, flags, order=order)
     torch.cuda.synchronize()
     with pytest.raises(RuntimeError, match="out-of-range index"):
         L.check_device_status(cuda)

@@ -265,7 +265,12 @@ k_conv_tc(const T* __restrict__ F, int64_t n_in, int c_in, const T* __restrict__
   if (tid < KMAX) s_klist[tid] = 0;
   if (tid < BM) {
     const int64_t t = tile0 + tid;
-    s_orow[tid] = t < n_out ? (perm != nullptr ? __ldg(&perm[t]) : static_cast<int32_t>(t)) : -1;
+    int32_t ov = t < n_out ? (perm != nullptr ? __ldg(&perm[t]) : static_cast<int32_t>(t)) : -1;
+    if (t < n_out && static_cast<int64_t>(static_cast<uint32_t>(ov)) >= n_out) {
+      raise_status(status, TSC_STATUS_INTERNAL);  // a row order that is not a permutation of the rows
+      ov = -1;
+    }
+    s_orow[tid] = ov;
   }
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
