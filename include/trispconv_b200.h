@@ -260,12 +260,16 @@ TSC_API int tsc_gather_from_pairs(const int64_t* pairs_in, const int64_t* pairs_
  * their count from meta[TSC_META_N_OVERFLOW] on the device.  Pass NULL when
  * the map cannot have any (submanifold maps).  row_order (NULL = identity)
  * is a permutation of [0, n_out) giving the order in which output rows are
- * grouped into tiles; results do not depend on it.  16-bit dtypes with KRSC
- * weights, C_in % 8 == 0 (or C_in % 4 == 0 and C_in <= 16), C_out % 8 == 0
- * and K <= 64 run on the tensor cores (mma.sync); with TSC_CONV_USE_TC,
+ * grouped into tiles; results do not depend on it (an entry outside
+ * [0, n_out) sets TSC_STATUS_INTERNAL and no row is written for it).
+ * Kernels, for 16-bit dtypes with KRSC weights: with TSC_CONV_USE_TC,
  * layers with C_in % 64 == 0, C_out % 32 == 0 and K <= 27 run on the
- * persistent tcgen05/TMEM kernel instead.  Everything else runs on the CUDA
- * cores.  tile_counter (NULL allowed) is one device uint32 through which the
+ * persistent tcgen05/TMEM kernel; C_in in {4, 8} with C_out in {16, 32, 64},
+ * or C_in in {16, 32} with C_out in {16, 32} (K <= 64), on the
+ * register-gather mma.sync kernel (TSC_CONV_NO_RG: not); other shapes with
+ * C_in % 8 == 0 (or C_in % 4 == 0 and C_in <= 16), C_out % 8 == 0 and
+ * K <= 64 on the shared-memory mma.sync kernel.  Everything else runs on the
+ * CUDA cores.  tile_counter (NULL allowed) is one device uint32 through which the
  * persistent kernel's CTAs take tiles dynamically (the call zeroes it on
  * `stream`); calls that may run concurrently need distinct counters.  With
  * NULL, tiles are dealt round robin. */
